@@ -1,0 +1,554 @@
+"""Benchmark of the grammar-masked selection hot path on B200.
+
+Default workload (the headline metric): masked argmax over bf16 logits [64, 128256] with
+per-row uint32 token bitmasks [64, 4008] (density U[0.5%, 20%]). A step is one kernel
+launch over one 64-row batch. Sixteen distinct input sets (279 MB, more than twice the
+126 MB L2) are rotated so every step streams its batch from HBM; the K timed steps are
+replayed from CUDA graphs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload batched|spec_verify|table_gather|scaling|vocab_parallel]
+
+One process per GPU (torchrun for N > 1). Batches shard over ranks with no communication
+("weak" scaling) except ``vocab_parallel``, which splits the vocabulary and all-gathers
+8-byte keys through NCCL. Rank 0 prints one JSON line.
+
+``--impl reference`` times the reference's own selection semantics on the host cores: the
+CPU oracle (a C restatement of the reference's mask + first-max selection, OpenMP over
+rows, every core the process may use), on the same workload and metric, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "masked-argmax rows/s and HBM GB/s (vs ~8 TB/s), B=64 V=128256 bf16"
+UNIT = "rows/s"
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from an ncu capture of the
+# dominant kernel (profiles/masked_select_batched_bf16.md); None until captured.
+NCU_TRAFFIC_PER_LAUNCH: dict[str, float | None] = {"batched": None}
+
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ---------------------------------------------------------------------------------------
+# workload definitions (bytes follow the algorithmic count: every logit once, every mask
+# word once, the outputs)
+# ---------------------------------------------------------------------------------------
+WORKLOADS = {
+    "batched": dict(rows=64, vocab=128256, desc="masked argmax bf16 [64,128256], mask u32 [64,4008]"),
+    "table_gather": dict(rows=256, vocab=128256,
+                         desc="DFA table gather + masked argmax: table u32 [4096,4008], bf16 [256,128256]"),
+    "spec_verify": dict(rows=32, vocab=151936, gamma=4,
+                        desc="spec verify bf16 [32,5,151936], masks u32 [32,5,4748], drafts i32 [32,4]"),
+    "scaling": dict(rows=128, vocab=256000,
+                    desc="batch-sharded masked argmax bf16 [128/GPU,256000] at 5% density"),
+    "vocab_parallel": dict(rows=1024, vocab=256000,
+                           desc="vocabulary-sharded masked argmax bf16 [1024,256000/N] + NCCL all-gather"),
+}
+
+
+def bytes_per_row(name: str, world: int = 1) -> float:
+    w = WORKLOADS[name]
+    v = w["vocab"]
+    words = (v + 31) // 32
+    if name == "spec_verify":
+        g1 = w["gamma"] + 1
+        return g1 * (v * 2 + words * 4) + w["gamma"] * 4 + 12
+    if name == "table_gather":
+        return words * 4 + 4 + v * 2 + 8
+    if name == "vocab_parallel":
+        return (v * 2 + words * 4) / world + 8 + 8
+    return v * 2 + words * 4 + 8
+
+
+# ---------------------------------------------------------------------------------------
+def _peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(p.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while the timed region runs."""
+
+    def __init__(self, device_index: int, period_s: float = 0.002) -> None:
+        self.samples: list[tuple[int, int]] = []
+        self.period = period_s
+        self._stop = threading.Event()
+        self._thread = None
+        self.max_mhz = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            uuid = None
+            try:
+                import torch
+
+                uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            except Exception:
+                pass
+            self._h = None
+            if uuid:
+                try:
+                    self._h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid).encode())
+                except Exception:
+                    self._h = None
+            if self._h is None:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+
+    def _run(self) -> None:
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((sm, reasons))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if self._nvml is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        nv = self._nvml
+        names = {
+            "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+            "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+            "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+            "display_clock_setting": 0x100,
+        }
+        seen = 0
+        for _, r in self.samples:
+            seen |= r
+        mhz = sorted(s for s, _ in self.samples)
+        del nv
+        return {
+            "sm_mhz": mhz[len(mhz) // 2],
+            "sm_max_mhz": self.max_mhz,
+            "reasons": [k for k, bit in names.items() if seen & bit],
+            "samples": len(self.samples),
+        }
+
+
+# ---------------------------------------------------------------------------------------
+# CPU reference arm / CPU baseline
+# ---------------------------------------------------------------------------------------
+def _cpu_inputs(name: str):
+    from onyx_b200 import workloads
+
+    if name in ("batched",):
+        w = workloads.batched()
+        return w
+    if name == "table_gather":
+        return workloads.table_gather()
+    if name == "scaling":
+        return workloads.scaling(rows=128)
+    if name == "vocab_parallel":
+        return workloads.scaling(rows=128)
+    raise ValueError(name)
+
+
+def cpu_measure(name: str, budget_s: float, steps: int | None = None, warmup: int = 0):
+    """Time the oracle (C, OpenMP over rows, all usable cores) on this workload.
+
+    Returns (rows/s, threads, sample description, seconds, rows processed)."""
+    import oracle
+
+    threads = oracle.default_threads()
+    oracle.load()
+    if name == "spec_verify":
+        from onyx_b200 import workloads
+
+        w = workloads.spec_verify(lambda x, m: oracle.masked_argmax(x, m, dtype="bf16", threads=threads)[0])
+
+        def run_once():
+            oracle.spec_verify(w["logits_bf16"], w["masks"], w["drafts"], dtype="bf16", threads=threads)
+
+        rows_per_call = w["logits_bf16"].shape[0]
+        what = "spec verify of 32 entries x 5 rows x 151936 bf16"
+    else:
+        w = _cpu_inputs(name)
+        if name == "table_gather":
+            def run_once():
+                oracle.gather_masked_argmax(w["logits_bf16"], w["table"], w["state_ids"],
+                                            dtype="bf16", threads=threads)
+            rows_per_call = w["logits_bf16"].shape[0]
+            what = "table gather + masked argmax of 256 rows x 128256 bf16"
+        else:
+            def run_once():
+                oracle.masked_argmax(w["logits_bf16"], w["masks"], dtype="bf16", threads=threads)
+            rows_per_call = w["logits_bf16"].shape[0]
+            what = f"masked argmax of {rows_per_call} rows x {w['logits_bf16'].shape[1]} bf16"
+    for _ in range(warmup):
+        run_once()
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        run_once()
+        n += 1
+        el = time.perf_counter() - t0
+        if steps is not None:
+            if n >= steps or el > budget_s:
+                break
+        elif el > budget_s and n >= 2:
+            break
+    el = time.perf_counter() - t0
+    rows = n * rows_per_call
+    return rows / el, threads, f"{n} calls of {what} ({rows} rows, {el:.1f} s)", el, rows
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    # bounded: each step is one call over the workload's batch; the run stops early once
+    # about 60 s of CPU work is done, so any --steps finishes within minutes
+    value, threads, sample, el, rows = cpu_measure(args.workload, budget_s=60.0,
+                                                   steps=args.steps, warmup=min(args.warmup, 3))
+    line = {
+        "impl": "reference",
+        "metric": METRIC if args.workload == "batched" else f"{args.workload} rows/s",
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded, shapes and distributions of the workload)",
+        "config": {"workload": args.workload, "desc": WORKLOADS[args.workload]["desc"]},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------------------
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from onyx_b200 import masked_selection as ms
+    from onyx_b200 import vocab_parallel, workloads
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and world > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    distributed = world > 1
+    if distributed:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    name = args.workload
+    spec = WORKLOADS[name]
+    props = torch.cuda.get_device_properties(dev)
+    l2 = int(getattr(props, "L2_cache_size", 126 * 2**20))
+
+    def bf16(a):
+        return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).to(dev).view(torch.bfloat16)
+
+    def words(a):
+        return torch.from_numpy(np.ascontiguousarray(a, dtype=np.uint32).view(np.int32)).to(dev)
+
+    # ---- inputs, one seeded set copied into R rotating device buffers -------------------
+    seed_shift = 17 * rank
+    if name == "batched":
+        w = workloads.batched(seed=workloads.SEEDS[2] + seed_shift)
+        host_in = {"x": w["logits_bf16"], "m": w["masks"]}
+    elif name == "table_gather":
+        w = workloads.table_gather(seed=workloads.SEEDS[4] + seed_shift)
+        host_in = {"x": w["logits_bf16"], "ids": w["state_ids"]}
+        table = words(w["table"])
+    elif name == "spec_verify":
+        def gpu_argmax(x, m):
+            r = ms.masked_argmax(bf16(x), words(m))
+            return r.token_ids.cpu().numpy()
+        w = workloads.spec_verify(gpu_argmax, seed=workloads.SEEDS[3] + seed_shift)
+        host_in = {"x": w["logits_bf16"], "m": w["masks"], "d": w["drafts"]}
+    elif name == "scaling":
+        w = workloads.scaling(seed=workloads.SEEDS[5] + seed_shift, rows=spec["rows"])
+        host_in = {"x": w["logits_bf16"], "m": w["masks"]}
+    elif name == "vocab_parallel":
+        w = workloads.scaling(seed=workloads.SEEDS[5], rows=spec["rows"])
+        lo, hi = vocab_parallel.vocab_shard_bounds(spec["vocab"], rank, world)
+        host_in = {"x": np.ascontiguousarray(w["logits_bf16"][:, lo:hi]),
+                   "m": np.ascontiguousarray(w["masks"][:, lo // 32 : (hi + 31) // 32])}
+        col_offset = lo
+    else:
+        raise SystemExit(f"unknown workload {name}")
+    set_bytes = sum(v.nbytes for v in host_in.values())
+    R = max(2, math.ceil(2 * l2 / set_bytes) + 1)
+    bufs = []
+    for _ in range(R):
+        b = {}
+        for k, v in host_in.items():
+            if k == "x":
+                b[k] = bf16(v)
+            elif k in ("m",):
+                b[k] = words(v)
+            else:
+                b[k] = torch.from_numpy(np.ascontiguousarray(v)).to(dev)
+        bufs.append(b)
+    rows_per_step = spec["rows"]
+
+    def step(k: int):
+        b = bufs[k % R]
+        if name in ("batched", "scaling"):
+            return ms.masked_argmax(b["x"], b["m"])
+        if name == "table_gather":
+            return ms.gather_masked_argmax(b["x"], table, b["ids"])
+        if name == "spec_verify":
+            return ms.spec_verify(b["x"], b["m"], b["d"])
+        if name == "vocab_parallel":
+            return vocab_parallel.vocab_parallel_masked_argmax(b["x"], b["m"], col_offset)
+        raise AssertionError
+
+    launches_per_step = 1 if name != "vocab_parallel" else 2
+
+    # ---- graphs of steps (the collective path is replayed eagerly) ----------------------
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for k in range(R):
+            step(k)  # warm the workspace for this stream and load the library
+    stream.synchronize()
+    use_graphs = name != "vocab_parallel"
+    chunk = min(args.steps, 1024)
+
+    def make_graph(n: int):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for k in range(n):
+                step(k)
+        return g
+
+    if use_graphs:
+        g_main = make_graph(chunk)
+        rem = args.steps % chunk
+        g_rem = make_graph(rem) if rem else None
+        reps = args.steps // chunk
+
+    def run_steps(n_steps: int):
+        # untimed: whole graph replays covering at least n_steps steps
+        if use_graphs:
+            with torch.cuda.stream(stream):
+                for _ in range(max(1, math.ceil(n_steps / chunk))):
+                    g_main.replay()
+        else:
+            with torch.cuda.stream(stream):
+                for k in range(n_steps):
+                    step(k)
+
+    # ---- pre-heat (clocks up) + warm-up ------------------------------------------------
+    t_end = time.perf_counter() + 0.5
+    while time.perf_counter() < t_end:
+        run_steps(chunk if use_graphs else 16)
+        stream.synchronize()
+    run_steps(args.warmup)
+    stream.synchronize()
+
+    # ---- timed region -------------------------------------------------------------------
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if distributed:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        if use_graphs:
+            with torch.cuda.stream(stream):
+                for _ in range(reps):
+                    g_main.replay()
+                if g_rem is not None:
+                    g_rem.replay()
+        else:
+            run_steps(args.steps)
+        end.record(stream)
+        end.synchronize()
+    torch.cuda.synchronize(dev)
+    if distributed:
+        dist.barrier()
+    ms_total = start.elapsed_time(end)
+    t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
+    if distributed:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total = float(t.item())
+    ms_per_step = ms_total / args.steps
+    total_rows = rows_per_step * args.steps * (world if name != "vocab_parallel" else 1)
+    value = total_rows / (ms_total / 1e3)
+
+    # ---- roofline of the dominant kernel ------------------------------------------------
+    per_launch_bytes = bytes_per_row(name, world) * rows_per_step
+    achieved = per_launch_bytes / (ms_per_step / 1e3) / 1e9
+    peak, peak_kind = _peaks()
+    roofline = {
+        "bound": "hbm",
+        "achieved": achieved,
+        "peak": peak,
+        "unit": "GB/s",
+        "frac": achieved / peak,
+        "traffic": NCU_TRAFFIC_PER_LAUNCH.get(name),
+        "peak_source": f"MEASURED_PEAKS.json hbm_gbs (of {peak_kind})",
+        "algorithmic_bytes_per_launch": per_launch_bytes,
+    }
+
+    # ---- end to end through the public API with host buffers ---------------------------
+    e2e_steps = args.steps if name != "vocab_parallel" else min(args.steps, 50)
+    e2e_steps = min(e2e_steps, max(20, int(2000 * 17.5e6 / max(set_bytes, 1))))
+    def _host_view(k, v):
+        v = np.ascontiguousarray(v)
+        if k == "x":
+            return v.view(np.int16)
+        return v.view(np.int32) if v.dtype == np.uint32 else v
+
+    pinned = {k: torch.from_numpy(_host_view(k, v)).pin_memory() for k, v in host_in.items()}
+    out_host = torch.empty((2, rows_per_step), dtype=torch.int32).pin_memory()
+    dev_in = {k: torch.empty(v.shape, dtype=v.dtype, device=dev) for k, v in pinned.items()}
+    h2d = sum(v.numel() * v.element_size() for v in pinned.values())
+    d2h = out_host.numel() * 4
+
+    def e2e_step():
+        for k, v in pinned.items():
+            dev_in[k].copy_(v, non_blocking=True)
+        xin = dev_in["x"].view(torch.bfloat16)
+        if name in ("batched", "scaling"):
+            r = ms.masked_argmax(xin, dev_in["m"])
+            out = (r.token_ids, r.status)
+        elif name == "table_gather":
+            r = ms.gather_masked_argmax(xin, table, dev_in["ids"])
+            out = (r.token_ids, r.status)
+        elif name == "spec_verify":
+            r = ms.spec_verify(xin, dev_in["m"], dev_in["d"])
+            out = (r.accept_len, r.correction)
+        else:
+            r = vocab_parallel.vocab_parallel_masked_argmax(xin, dev_in["m"], col_offset)
+            out = (r.token_ids, r.status)
+        out_host[0].copy_(out[0], non_blocking=True)
+        out_host[1].copy_(out[1], non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            e2e_step()
+    stream.synchronize()
+    if distributed:
+        dist.barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e_start.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e_end.record(stream)
+    e_end.synchronize()
+    et = torch.tensor([e_start.elapsed_time(e_end)], dtype=torch.float64, device=dev)
+    if distributed:
+        dist.all_reduce(et, op=dist.ReduceOp.MAX)
+    e2e_rows = rows_per_step * e2e_steps * (world if name != "vocab_parallel" else 1)
+    e2e_value = e2e_rows / (float(et.item()) / 1e3)
+
+    # ---- CPU baseline (rank 0, N=1 only) -----------------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, threads, sample, _, _ = cpu_measure(name, budget_s=args.cpu_seconds)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+
+    if distributed:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    clock = clocks.summary()
+    line = {
+        "metric": METRIC if name == "batched" else f"{name} rows/s",
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak" if name != "vocab_parallel" else "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,3) bf16 logits, Bernoulli token bitmasks)",
+        "config": {
+            "workload": name,
+            "desc": spec["desc"],
+            "rows_per_step_per_gpu": rows_per_step,
+            "parallelism": (f"batch-sharded x{world}" if name != "vocab_parallel"
+                            else f"vocab-sharded x{world}"),
+            "l2_policy": f"{R} rotating input sets ({R * set_bytes / 1e6:.0f} MB > 2 x L2 "
+                         f"{l2 / 1e6:.0f} MB)",
+            "timing": "CUDA events on the launching stream, CUDA-graph replay of the steps, max over ranks",
+        },
+        "gbs": achieved,
+        "roofline": roofline,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+        "cpu_baseline": cpu,
+        "gpu_launches": args.steps * launches_per_step,
+        "clocks": clock,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="batched")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

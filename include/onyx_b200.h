@@ -1,0 +1,153 @@
+/*
+ * onyx_b200 -- C ABI of the B200 (sm_100a) grammar-masked selection library.
+ *
+ * Plain pointers and sizes only: every buffer is caller-owned device memory, `stream` is a
+ * cudaStream_t passed as void* (NULL = legacy default stream), and no call allocates,
+ * synchronises or retains a pointer. Launches are asynchronous; per-row data errors are
+ * reported through the status outputs, launch/argument errors through the return code.
+ *
+ * Token-mask layout (the bitmask convention of this library): token id t of a row is valid
+ * iff bit (t & 31) of word (t >> 5) is set, words little-endian uint32, W = ceil(V/32)
+ * words per row, bits at ids >= V ignored. The reference passes the same set as a sorted
+ * tuple of ids (onyx_cuda/src/onyx_cuda/torch_grammar_mask.py:69-86, :399-422).
+ *
+ * Selection semantics (shared by every entry point): the masked row keeps valid values and
+ * is -inf elsewhere (torch_grammar_mask.py:145-186); the selected id is the lowest index
+ * holding the maximum under float comparison (-0.0 == +0.0, +inf ties resolve low;
+ * onyx_cuda/src/onyx_cuda/torch_backend.py:970-1007, generation.py:212-224).
+ *
+ * Workspace: entry points that split one row over several CTAs need a caller-owned device
+ * workspace of the size returned by the matching *_workspace_size function (0 means none
+ * is needed and NULL may be passed). It must be 256-byte aligned and zero-filled before its
+ * first use; every call leaves it zero-filled again. Calls that may run concurrently (other
+ * streams) need separate workspaces.
+ */
+#ifndef ONYX_B200_H_
+#define ONYX_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ONYX_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define ONYX_API __attribute__((visibility("default")))
+#else
+#define ONYX_API
+#endif
+
+/* dtype codes */
+#define ONYX_DTYPE_F32 0
+#define ONYX_DTYPE_F16 1
+#define ONYX_DTYPE_BF16 2
+#define ONYX_DTYPE_F64 3
+
+/* return codes */
+#define ONYX_OK 0
+#define ONYX_ERR_INVALID_ARGUMENT 1
+#define ONYX_ERR_UNSUPPORTED_DTYPE 2
+#define ONYX_ERR_WORKSPACE 3
+#define ONYX_ERR_CUDA 4
+
+/* per-row status bits */
+#define ONYX_STATUS_EMPTY_MASK 1u     /* no valid token: grammar no-decision
+                                         (grammar_selection.py:122-127) */
+#define ONYX_STATUS_ALL_NEG_INF 2u    /* valid tokens exist but every value is -inf:
+                                         rejected by torch_grammar_mask.py:182-185 */
+#define ONYX_STATUS_NAN_IN_SUPPORT 4u /* a valid value is NaN: rejected by
+                                         torch_backend.py:991-996 */
+#define ONYX_STATUS_BAD_STATE 8u      /* gather: DFA state id outside the table */
+
+ONYX_API int onyx_abi_version(void);
+ONYX_API const char* onyx_error_string(int code);
+/* cudaError_t of the last failed launch on this host thread */
+ONYX_API int onyx_last_cuda_error(void);
+
+/*
+ * Masked greedy selection over `rows` rows of `vocab` logits.
+ * Replaces TorchCUDAGrammarLogitMask.apply + select_cuda_argmax for a whole batch
+ * (onyx_cuda/src/onyx_cuda/torch_grammar_mask.py:69-86 and torch_backend.py:970-1007).
+ * logits: rows x vocab, row r at logits + r*row_stride elements (dtype code).
+ * mask:   rows x mask_stride words, or NULL to select over every column (the plain
+ *         select_cuda_argmax contract: NaN rejected, first maximum).
+ * out_idx[r]: selected id (int32), -1 on EMPTY_MASK / NAN_IN_SUPPORT; on ALL_NEG_INF the
+ *             lowest valid id. out_status[r]: status bits.
+ */
+ONYX_API size_t onyx_masked_argmax_workspace_size(int64_t rows, int64_t vocab, int dtype);
+ONYX_API int onyx_masked_argmax(const void* logits, int dtype, int64_t rows, int64_t vocab,
+                       int64_t row_stride, const uint32_t* mask, int64_t mask_stride,
+                       int32_t* out_idx, uint32_t* out_status, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/*
+ * Fused per-DFA-state mask-table gather + masked greedy selection: row r uses mask row
+ * table[state_ids[r]] (n_states rows of table_stride words). The table is the reference's
+ * valid-id scan (onyx_cuda/rust/src/regex_runtime.rs:129-145) precomputed per state, so this
+ * replaces get_valid_token_ids + apply + select for a batch. Ids outside [0, n_states)
+ * give BAD_STATE. Uses the masked-argmax workspace size.
+ */
+ONYX_API int onyx_gather_masked_argmax(const void* logits, int dtype, int64_t rows, int64_t vocab,
+                              int64_t row_stride, const uint32_t* table, int64_t n_states,
+                              int64_t table_stride, const int32_t* state_ids, int32_t* out_idx,
+                              uint32_t* out_status, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/*
+ * Grammar-aware speculative verify of `batch` entries with `gamma` draft tokens each.
+ * Row (b,i), i in [0,gamma], is logits + b*batch_stride + i*row_stride with mask
+ * masks + b*mask_batch_stride + i*mask_row_stride; drafts[b*draft_stride + i], i < gamma.
+ * accept_len[b] = first i < gamma whose masked selection differs from the draft (else
+ * gamma); correction[b] = that selection, or on full acceptance the selection of row gamma
+ * when bonus != 0 (onyx_cuda grammar_continuation.py:127-152), else -1 (macOS loop without
+ * bonus, onyx/speculative.py:545-608). A row with a status bit ends the decision at that
+ * row: accept_len = i, correction = -1, out_status[b] = the row's bits
+ * (grammar_acceptance.py:196-283). Replaces decide_match_replace_acceptance /
+ * decide_grammar_masked_target_acceptance (acceptance.py:96-132, grammar_acceptance.py:166).
+ * gamma in [1, 255].
+ */
+ONYX_API size_t onyx_spec_verify_workspace_size(int64_t batch, int64_t gamma, int64_t vocab, int dtype);
+ONYX_API int onyx_spec_verify(const void* logits, int dtype, int64_t batch, int64_t gamma, int64_t vocab,
+                     int64_t batch_stride, int64_t row_stride, const uint32_t* masks,
+                     int64_t mask_batch_stride, int64_t mask_row_stride, const int32_t* drafts,
+                     int64_t draft_stride, int bonus, int32_t* accept_len, int32_t* correction,
+                     uint32_t* out_status, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/*
+ * Materialise masked rows: out = valid values bit-for-bit, -inf elsewhere; out_status gets
+ * EMPTY_MASK / ALL_NEG_INF (TorchCUDAGrammarLogitMask._apply_device_indices,
+ * torch_grammar_mask.py:145-186). `out` must not alias `logits`.
+ */
+ONYX_API size_t onyx_mask_apply_workspace_size(int64_t rows, int64_t vocab, int dtype);
+ONYX_API int onyx_mask_apply(const void* logits, int dtype, int64_t rows, int64_t vocab,
+                    int64_t row_stride, const uint32_t* mask, int64_t mask_stride, void* out,
+                    int64_t out_stride, uint32_t* out_status, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/*
+ * Vocabulary-parallel selection, step 1: this rank's column shard [col_offset,
+ * col_offset + shard_vocab) of every row (col_offset a multiple of 32; the mask words are
+ * the shard's own). out_keys[r] packs (order code of the maximum << 32) | (0xFFFFFFFF -
+ * global id); 0 means no valid token in the shard. Gather the keys of all shards (e.g.
+ * NCCL all-gather) and combine with onyx_combine_partials. Not for f64.
+ * No counterpart in the reference (single device only); it splits select_cuda_argmax's
+ * reduction over GPUs with identical results.
+ */
+ONYX_API size_t onyx_vocab_partial_workspace_size(int64_t rows, int64_t shard_vocab, int dtype);
+ONYX_API int onyx_vocab_partial_argmax(const void* logits, int dtype, int64_t rows, int64_t shard_vocab,
+                              int64_t row_stride, const uint32_t* mask, int64_t mask_stride,
+                              int64_t col_offset, uint64_t* out_keys, void* workspace,
+                              size_t workspace_bytes, void* stream);
+/* step 2: keys[part*rows + r] for n_parts shards -> out_idx / out_status as masked argmax */
+ONYX_API int onyx_combine_partials(const uint64_t* keys, int64_t n_parts, int64_t rows, int32_t* out_idx,
+                          uint32_t* out_status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ONYX_B200_H_ */
