@@ -398,7 +398,12 @@ __device__ void finalize_group(const ScanParams& p, int64_t group, const Partial
     const Partial* base = p.ws_part + group * (int64_t)P * p.segs;
     for (int i = warp; i < P; i += nwarps) {
       Partial acc = empty_partial();
-      for (int s = lane; s < p.segs; s += 32) merge(acc, ld_partial_cg(base + (int64_t)i * p.segs + s));
+      for (int s = lane; s < p.segs; s += 32) {
+        Partial* slot = const_cast<Partial*>(base) + (int64_t)i * p.segs + s;
+        merge(acc, ld_partial_cg(slot));
+        // leave the workspace zero-filled: the next call may lay it out differently
+        __stcg(reinterpret_cast<ulonglong2*>(slot), make_ulonglong2(0ull, 0ull));
+      }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         Partial other;

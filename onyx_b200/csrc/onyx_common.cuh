@@ -129,14 +129,23 @@ __device__ __forceinline__ float max_nan_f32(float a, float b) {
   return d;
 }
 
+// PTX prmt in its default mode: bit 3 of a selector nibble replicates the selected
+// byte's most significant bit over the whole byte. (__byte_perm only honours the low
+// three bits of each nibble, so it cannot express this.)
+__device__ __forceinline__ uint32_t prmt_sign(uint32_t a, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(d) : "r"(a), "r"(sel));
+  return d;
+}
+
 // Expand 4 mask bits (b0..b3) into per-16-bit-lane masks for two packed registers:
-// returns lo = [b0 b0 b1 b1] bytes, hi = [b2 b2 b3 b3] bytes (0x00 or 0xFF each).
+// m01 = [b0 b0 b1 b1] bytes, m23 = [b2 b2 b3 b3] bytes (0x00 or 0xFF each).
 // The multiply moves bit k to bit 8k+7 without carries; prmt then sign-replicates the
 // selected bytes.
 __device__ __forceinline__ void expand4_16(uint32_t nib, uint32_t& m01, uint32_t& m23) {
   const uint32_t s = (nib & 0xFu) * 0x10204080u;
-  m01 = __byte_perm(s, 0u, 0x9988u);
-  m23 = __byte_perm(s, 0u, 0xBBAAu);
+  m01 = prmt_sign(s, 0x9988u);
+  m23 = prmt_sign(s, 0xBBAAu);
 }
 
 // 16-bit float helpers (bit pattern -> float)

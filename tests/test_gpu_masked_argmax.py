@@ -201,3 +201,19 @@ def test_results_are_independent_of_the_stream(cuda_lib):
         other = ms.masked_argmax(x, m)
     s.synchronize()
     assert torch.equal(ref.token_ids, other.token_ids) and torch.equal(ref.status, other.status)
+
+
+def test_workspace_is_left_zeroed_across_layouts(cuda_lib):
+    """Calls of different shapes share one workspace per stream; each must leave it zeroed
+    (counters, flags and partials), whatever layout the previous call used."""
+    rng = np.random.default_rng(12)
+    for rows, vocab, dtype in ((4, 16385, "f64"), (4, 40000, "bf16"), (64, 128256, "bf16"),
+                               (3, 151665, "f32"), (1, 256000, "f16"), (7, 99999, "bf16")):
+        x, m = _random_case(rng, rows, vocab, dtype, 0.05)
+        idx_ref, st_ref = oracle.masked_argmax(x, m, dtype=dtype)
+        r = ms.masked_argmax(to_device(x, dtype), masks_to_device(m))
+        _check(r.token_ids, r.status, idx_ref, st_ref)
+        out, st = ms.mask_apply(to_device(x, dtype), masks_to_device(m))
+        torch.cuda.synchronize()
+        for buf in ms._WORKSPACES._buffers.values():
+            assert int(torch.count_nonzero(buf)) == 0
