@@ -382,7 +382,7 @@ def run_ours(args) -> None:
                     step(k)
 
     # ---- pre-heat (clocks up) + warm-up ------------------------------------------------
-    t_end = time.perf_counter() + 0.5
+    t_end = time.perf_counter() + args.preheat_seconds
     while time.perf_counter() < t_end:
         run_steps(chunk if use_graphs else 16)
         stream.synchronize()
@@ -541,6 +541,8 @@ def main() -> None:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="batched")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--preheat-seconds", type=float, default=0.5,
+                    help="untimed replays before the warm-up, to bring the SM clock up")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -29,6 +29,10 @@
 #include <algorithm>
 #include <cstdlib>
 
+#ifndef ONYX_PDL_EARLY
+#define ONYX_PDL_EARLY 0
+#endif
+
 namespace onyx {
 
 enum Mode : int { kModeArgmax = 0, kModeKey = 1, kModeVerify = 2 };
@@ -63,69 +67,11 @@ struct ScanParams {
 };
 
 constexpr int kMaxPerGroup = 256;
-
-template <int THREADS>
-__device__ __forceinline__ uint32_t cta_max_u32(uint32_t v, uint32_t* scratch) {
-  v = __reduce_max_sync(0xFFFFFFFFu, v);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) scratch[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    uint32_t w = lane < THREADS / 32 ? scratch[lane] : 0u;
-    w = __reduce_max_sync(0xFFFFFFFFu, w);
-    if (lane == 0) scratch[32] = w;
-  }
-  __syncthreads();
-  uint32_t r = scratch[32];
-  __syncthreads();
-  return r;
-}
-
-template <int THREADS>
-__device__ __forceinline__ uint32_t cta_min_u32(uint32_t v, uint32_t* scratch) {
-  v = __reduce_min_sync(0xFFFFFFFFu, v);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) scratch[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    uint32_t w = lane < THREADS / 32 ? scratch[lane] : 0xFFFFFFFFu;
-    w = __reduce_min_sync(0xFFFFFFFFu, w);
-    if (lane == 0) scratch[32] = w;
-  }
-  __syncthreads();
-  uint32_t r = scratch[32];
-  __syncthreads();
-  return r;
-}
-
-template <int THREADS>
-__device__ __forceinline__ unsigned long long cta_max_u64(unsigned long long v,
-                                                          unsigned long long* scratch) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, v, o);
-    v = other > v ? other : v;
-  }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) scratch[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    unsigned long long w = lane < THREADS / 32 ? scratch[lane] : 0ull;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, w, o);
-      w = other > w ? other : w;
-    }
-    if (lane == 0) scratch[32] = w;
-  }
-  __syncthreads();
-  unsigned long long r = scratch[32];
-  __syncthreads();
-  return r;
-}
+constexpr uint32_t kFull = 0xFFFFFFFFu;
 
 // ---------------------------------------------------------------------------------------
-// fast path: 16-byte aligned rows of bf16 / f16 / f32
+// fast path: 16-byte aligned rows of bf16 / f16 / f32. One warp owns one segment of
+// 32 lanes x UNROLL vectors; every load of the segment is issued before any is consumed.
 // ---------------------------------------------------------------------------------------
 template <int DT>
 struct Vec16;
@@ -141,7 +87,7 @@ struct Packed16 {
   __device__ static float half_to_f32(uint32_t h) {
     return DT == kBF16 ? bf16_bits_to_f32(h) : f16_bits_to_f32(h);
   }
-  // masked maximum of one vector (8 mask bits in `bits`), as a float; -inf if no bit set
+  // masked maximum of one vector (8 mask bits in `bits`), as a packed pair
   __device__ static uint32_t masked_pair_max(const uint4& x, uint32_t bits) {
     uint32_t m01, m23, m45, m67;
     expand4_16(bits, m01, m23);
@@ -158,6 +104,25 @@ struct Packed16 {
   __device__ static float elem(const uint4& x, int j) {
     const uint32_t w = (j < 2) ? x.x : (j < 4) ? x.y : (j < 6) ? x.z : x.w;
     return half_to_f32((j & 1) ? (w >> 16) : (w & 0xFFFFu));
+  }
+  __device__ static float scalar(uint32_t raw) { return half_to_f32(raw); }
+  // the 16-bit pattern of a float that came from this type (exact)
+  __device__ static uint32_t from_f32(float f) {
+    if constexpr (DT == kBF16) {
+      return __float_as_uint(f) >> 16;
+    } else {
+      return __half_as_ushort(__float2half_rn(f));
+    }
+  }
+  // 0xFFFF in each 16-bit lane of a equal (as floats) to the same lane of b
+  __device__ static uint32_t eq_mask(uint32_t a, uint32_t b) {
+    uint32_t d;
+    if constexpr (DT == kBF16) {
+      asm("set.eq.u32.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    } else {
+      asm("set.eq.u32.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    }
+    return d;
   }
 };
 
@@ -182,110 +147,148 @@ struct Vec16<kF32> {
     const uint32_t w = (j == 0) ? x.x : (j == 1) ? x.y : (j == 2) ? x.z : x.w;
     return __uint_as_float(w);
   }
+  __device__ static float scalar(uint32_t raw) { return __uint_as_float(raw); }
 };
 
-template <int DT, int THREADS, int UNROLL>
-__device__ __forceinline__ Partial scan_segment_fast(const void* row_base, const uint32_t* mrow,
-                                                     int64_t e0, int64_t e1,
-                                                     uint32_t* scratch32) {
+// Masked maximum and its lowest index over elements [e0, e1) of one row, by one warp.
+template <int DT, int UNROLL>
+__device__ __forceinline__ Partial scan_warp_fast(const void* row_base, const uint32_t* mrow,
+                                                  int64_t e0, int64_t e1, int lane) {
   using V = Vec16<DT>;
   constexpr int E = V::kElems;
-  const int tid = threadIdx.x;
+  constexpr int kBytesPerElem = (DT == kF32) ? 4 : 2;
+  constexpr uint32_t kLaneBits = (E == 8) ? 0xFFu : 0xFu;
   const int64_t nv = (e1 - e0) / E;  // full vectors in this segment
   const int tail = (int)((e1 - e0) - nv * E);
   const char* rowc = static_cast<const char*>(row_base);
-  constexpr int kBytesPerElem = (DT == kF32) ? 4 : 2;
 
   uint4 x[UNROLL];
-  uint32_t bits[UNROLL];
+  uint32_t w[UNROLL];
 #pragma unroll
   for (int k = 0; k < UNROLL; ++k) {
-    const int64_t v = (int64_t)k * THREADS + tid;
+    const int64_t v = (int64_t)k * 32 + lane;
+    const int64_t e = e0 + v * E;
     if (v < nv) {
-      const int64_t e = e0 + v * E;
-      x[k] = ld_stream_v4(rowc + e * kBytesPerElem);
-      bits[k] = mrow ? (ld_mask_word(mrow + (e >> 5)) >> (e & 31)) : 0xFFFFFFFFu;
+      x[k] = __ldcs(reinterpret_cast<const uint4*>(rowc + e * kBytesPerElem));
+      w[k] = mrow ? __ldg(mrow + (e >> 5)) : 0xFFFFFFFFu;
     } else {
       x[k] = make_uint4(0u, 0u, 0u, 0u);
-      bits[k] = 0u;
+      w[k] = 0u;
     }
   }
-  // ragged end of the row (vocab not a multiple of the vector width): one scalar element
-  // per thread, at the highest indices of the segment
+  // ragged end of the row (vocab not a multiple of the vector width): one scalar
+  // element per lane, at the highest indices of the segment
   uint32_t tail_raw = 0u, tail_bit = 0u;
-  int64_t tail_e = 0;
-  if (tid < tail) {
-    tail_e = e0 + nv * E + tid;
+  const int64_t tail_e = e0 + nv * E + lane;
+  if (lane < tail) {
     if (DT == kF32) {
-      tail_raw = __float_as_uint(reinterpret_cast<const float*>(rowc)[tail_e]);
+      tail_raw = __float_as_uint(__ldg(reinterpret_cast<const float*>(rowc) + tail_e));
     } else {
-      tail_raw = reinterpret_cast<const uint16_t*>(rowc)[tail_e];
+      tail_raw = __ldg(reinterpret_cast<const unsigned short*>(rowc) + tail_e);
     }
-    tail_bit = mrow ? ((ld_mask_word(mrow + (tail_e >> 5)) >> (tail_e & 31)) & 1u) : 1u;
+    tail_bit = mrow ? ((__ldg(mrow + (tail_e >> 5)) >> (tail_e & 31)) & 1u) : 1u;
   }
 
-  // phase 1: masked maximum, no indices
-  constexpr uint32_t kLaneBits = (E == 8) ? 0xFFu : 0xFu;
+  // phase 1: masked maximum, no indices; each vector's own maximum is kept for phase 2
+  uint32_t bits[UNROLL];
   uint32_t any = tail_bit;
+#pragma unroll
+  for (int k = 0; k < UNROLL; ++k) {
+    const int64_t e = e0 + ((int64_t)k * 32 + lane) * E;
+    bits[k] = (w[k] >> (e & 31)) & kLaneBits;
+    any |= bits[k];
+  }
   float tmax;
+  uint32_t vmax[UNROLL];  // per-vector masked maximum (packed pair, or f32 bits)
   if constexpr (DT == kF32) {
     tmax = __int_as_float(0xFF800000);
 #pragma unroll
     for (int k = 0; k < UNROLL; ++k) {
-      any |= bits[k] & kLaneBits;
-      tmax = max_nan_f32(tmax, V::masked_max(x[k], bits[k]));
+      const float vm = V::masked_max(x[k], bits[k]);
+      vmax[k] = __float_as_uint(vm);
+      tmax = max_nan_f32(tmax, vm);
     }
-    if (tail_bit) tmax = max_nan_f32(tmax, __uint_as_float(tail_raw));
   } else {
     uint32_t pm = V::kNegInfPair;
 #pragma unroll
     for (int k = 0; k < UNROLL; ++k) {
-      any |= bits[k] & kLaneBits;
-      pm = V::pmax(pm, V::masked_pair_max(x[k], bits[k]));
+      vmax[k] = V::masked_pair_max(x[k], bits[k]);
+      pm = V::pmax(pm, vmax[k]);
     }
     tmax = V::pair_to_f32_max(pm);
-    if (tail_bit) tmax = max_nan_f32(tmax, V::half_to_f32(tail_raw));
   }
-  const uint32_t tord = ord32(tmax);
-  const int cta_any = __syncthreads_or(any != 0u);
-  const uint32_t M = cta_max_u32<THREADS>(tord, scratch32);
+  if (tail_bit) tmax = max_nan_f32(tmax, V::scalar(tail_raw));
+  // order code 0 = this lane holds no valid token
+  const uint32_t tord = any ? ord32(tmax) : 0u;
+  const uint32_t M = __reduce_max_sync(kFull, tord);
 
   Partial part;
-  part.flags = cta_any ? kFlagAny : 0u;
-  part.ord = cta_any ? (unsigned long long)M : 0ull;
+  part.flags = M ? kFlagAny : 0u;
+  part.ord = M;
   part.idx = 0xFFFFFFFFu;
-  if (!cta_any || M == kOrd32NaN) return part;
+  if (M == 0u || M == kOrd32NaN) return part;
 
-  // phase 2: first valid element equal to the CTA maximum
+  // phase 2 (only lanes holding the maximum): the first vector whose maximum equals M
+  // (a vector with valid elements reaches M only through a valid element equal to M),
+  // then the first valid element of that vector equal to M. Equality is float equality,
+  // so -0.0 and +0.0 match alike.
   uint32_t cand = 0xFFFFFFFFu;
-  if (any && tord == M) {
-    bool done = false;
+  if (tord == M) {
+    const float mf = __uint_as_float((M & 0x80000000u) ? (M & 0x7FFFFFFFu) : ~M);
+    int kk = -1;
+    uint4 xv = make_uint4(0u, 0u, 0u, 0u);
+    uint32_t bv = 0u;
+    if constexpr (DT == kF32) {
 #pragma unroll
-    for (int k = 0; k < UNROLL; ++k) {
-      if (done) break;
-      const uint32_t b = bits[k] & kLaneBits;
-      if (!b) continue;
-#pragma unroll
-      for (int j = 0; j < E; ++j) {
-        if (!done && ((b >> j) & 1u) && ord32(V::elem(x[k], j)) == M) {
-          cand = (uint32_t)(e0 + ((int64_t)k * THREADS + tid) * E + j);
-          done = true;
+      for (int k = UNROLL - 1; k >= 0; --k) {
+        if (bits[k] && __uint_as_float(vmax[k]) == mf) {
+          kk = k;
+          xv = x[k];
+          bv = bits[k];
         }
       }
+      if (kk >= 0) {
+        int j = 3;
+        if ((bv & 4u) && __uint_as_float(xv.z) == mf) j = 2;
+        if ((bv & 2u) && __uint_as_float(xv.y) == mf) j = 1;
+        if ((bv & 1u) && __uint_as_float(xv.x) == mf) j = 0;
+        cand = (uint32_t)(e0 + ((int64_t)kk * 32 + lane) * E + j);
+      }
+    } else {
+      const uint32_t h = V::from_f32(mf);
+      const uint32_t m2 = h | (h << 16);
+#pragma unroll
+      for (int k = UNROLL - 1; k >= 0; --k) {
+        if (bits[k] && V::eq_mask(vmax[k], m2)) {
+          kk = k;
+          xv = x[k];
+          bv = bits[k];
+        }
+      }
+      if (kk >= 0) {
+        uint32_t m01, m23, m45, m67;
+        expand4_16(bv, m01, m23);
+        expand4_16(bv >> 4, m45, m67);
+        // element j of the vector owns 16-bit lane j of the 64-bit words q (j < 4), r
+        const uint32_t q0 = V::eq_mask(xv.x, m2) & m01;
+        const uint32_t q1 = V::eq_mask(xv.y, m2) & m23;
+        const uint32_t q2 = V::eq_mask(xv.z, m2) & m45;
+        const uint32_t q3 = V::eq_mask(xv.w, m2) & m67;
+        const unsigned long long q = (unsigned long long)(q0 | ((unsigned long long)q1 << 32));
+        const unsigned long long r = (unsigned long long)(q2 | ((unsigned long long)q3 << 32));
+        const int j = q ? (__ffsll((long long)q) - 1) / 16 : 4 + (__ffsll((long long)r) - 1) / 16;
+        cand = (uint32_t)(e0 + ((int64_t)kk * 32 + lane) * E + j);
+      }
     }
-    if (!done && tail_bit) {
-      const float tv = (DT == kF32) ? __uint_as_float(tail_raw)
-                                    : Packed16<DT == kF32 ? kBF16 : DT>::half_to_f32(tail_raw);
-      if (ord32(tv) == M) cand = (uint32_t)tail_e;
-    }
+    if (kk < 0 && tail_bit && ord32(V::scalar(tail_raw)) == M) cand = (uint32_t)tail_e;
   }
-  part.idx = cta_min_u32<THREADS>(cand, scratch32);
+  part.idx = __reduce_min_sync(kFull, cand);
   return part;
 }
 
 // ---------------------------------------------------------------------------------------
 // generic path: any alignment, and f64. Scalar coalesced loads; phase 2 re-reads the
-// segment (it is still in L2).
+// segment (it is still in L1/L2).
 // ---------------------------------------------------------------------------------------
 template <int DT>
 __device__ __forceinline__ double load_elem(const void* base, int64_t i) {
@@ -309,33 +312,36 @@ __device__ __forceinline__ unsigned long long elem_ord(double v) {
   }
 }
 
-template <int DT, int THREADS>
-__device__ __forceinline__ Partial scan_segment_generic(const void* row_base,
-                                                        const uint32_t* mrow, int64_t e0,
-                                                        int64_t e1,
-                                                        unsigned long long* scratch64) {
-  const int tid = threadIdx.x;
-  unsigned long long tbest = 0ull;
-  uint32_t any = 0u;
-  for (int64_t e = e0 + tid; e < e1; e += THREADS) {
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(kFull, v, o);
+    v = other > v ? other : v;
+  }
+  return v;
+}
+
+template <int DT>
+__device__ __forceinline__ Partial scan_warp_generic(const void* row_base, const uint32_t* mrow,
+                                                     int64_t e0, int64_t e1, int lane) {
+  unsigned long long tbest = 0ull;  // 0 = no valid token seen by this lane
+  for (int64_t e = e0 + lane; e < e1; e += 32) {
     const uint32_t bit = mrow ? ((__ldg(mrow + (e >> 5)) >> (e & 31)) & 1u) : 1u;
     if (bit) {
-      any = 1u;
       const unsigned long long o = elem_ord<DT>(load_elem<DT>(row_base, e));
       tbest = o > tbest ? o : tbest;
     }
   }
-  const int cta_any = __syncthreads_or(any != 0u);
-  const unsigned long long M = cta_max_u64<THREADS>(tbest, scratch64);
+  const unsigned long long M = warp_max_u64(tbest);
   const unsigned long long nan_code = (DT == kF64) ? kOrd64NaN : (unsigned long long)kOrd32NaN;
   Partial part;
-  part.flags = cta_any ? kFlagAny : 0u;
-  part.ord = cta_any ? M : 0ull;
+  part.flags = M ? kFlagAny : 0u;
+  part.ord = M;
   part.idx = 0xFFFFFFFFu;
-  if (!cta_any || M == nan_code) return part;
+  if (M == 0ull || M == nan_code) return part;
   uint32_t cand = 0xFFFFFFFFu;
-  if (any && tbest == M) {
-    for (int64_t e = e0 + tid; e < e1; e += THREADS) {
+  if (tbest == M) {
+    for (int64_t e = e0 + lane; e < e1; e += 32) {
       const uint32_t bit = mrow ? ((__ldg(mrow + (e >> 5)) >> (e & 31)) & 1u) : 1u;
       if (bit && elem_ord<DT>(load_elem<DT>(row_base, e)) == M) {
         cand = (uint32_t)e;
@@ -343,7 +349,7 @@ __device__ __forceinline__ Partial scan_segment_generic(const void* row_base,
       }
     }
   }
-  part.idx = cta_min_u32<THREADS>(cand, reinterpret_cast<uint32_t*>(scratch64));
+  part.idx = __reduce_min_sync(kFull, cand);
   return part;
 }
 
@@ -382,101 +388,128 @@ __device__ __forceinline__ void st_partial(Partial* p, const Partial& v) {
   ulonglong2 w;
   w.x = v.ord;
   w.y = (unsigned long long)v.idx | ((unsigned long long)v.flags << 32);
-  *reinterpret_cast<ulonglong2*>(p) = w;
+  __stcg(reinterpret_cast<ulonglong2*>(p), w);
 }
 
+__device__ __forceinline__ Partial warp_merge(Partial acc) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    Partial other;
+    other.ord = __shfl_xor_sync(kFull, acc.ord, o);
+    other.idx = __shfl_xor_sync(kFull, acc.idx, o);
+    other.flags = __shfl_xor_sync(kFull, acc.flags, o);
+    merge(acc, other);
+  }
+  return acc;
+}
+
+// Combined result of member row `i` of a group: its `segs` partials, merged by one warp.
+// The partials are read once and zeroed, so every call leaves the workspace zero-filled
+// whatever layout the next call uses.
+__device__ __forceinline__ Partial reduce_member(Partial* base, int segs, int lane) {
+  Partial acc = empty_partial();
+  for (int s = lane; s < segs; s += 32) {
+    merge(acc, ld_partial_cg(base + s));
+    __stcg(reinterpret_cast<ulonglong2*>(base + s), make_ulonglong2(0ull, 0ull));
+  }
+  return warp_merge(acc);
+}
+
+// Outputs of one group, computed by one warp. `single` is the only partial when a group
+// has a single segment (no workspace).
 template <int MODE, bool IS64>
 __device__ void finalize_group(const ScanParams& p, int64_t group, const Partial* single,
-                               Partial* res /* smem [per_group] */) {
+                               int lane) {
   const int P = p.per_group;
-  if (single) {
-    if (threadIdx.x == 0) res[0] = *single;
-  } else {
-    // one warp per member row: reduce its `segs` partials
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nwarps = blockDim.x >> 5;
-    const Partial* base = p.ws_part + group * (int64_t)P * p.segs;
-    for (int i = warp; i < P; i += nwarps) {
-      Partial acc = empty_partial();
-      for (int s = lane; s < p.segs; s += 32) {
-        Partial* slot = const_cast<Partial*>(base) + (int64_t)i * p.segs + s;
-        merge(acc, ld_partial_cg(slot));
-        // leave the workspace zero-filled: the next call may lay it out differently
-        __stcg(reinterpret_cast<ulonglong2*>(slot), make_ulonglong2(0ull, 0ull));
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        Partial other;
-        other.ord = __shfl_xor_sync(0xFFFFFFFFu, acc.ord, o);
-        other.idx = __shfl_xor_sync(0xFFFFFFFFu, acc.idx, o);
-        other.flags = __shfl_xor_sync(0xFFFFFFFFu, acc.flags, o);
-        merge(acc, other);
-      }
-      if (lane == 0) res[i] = acc;
+  Partial* base = single ? nullptr : p.ws_part + group * (int64_t)P * p.segs;
+  if constexpr (MODE == kModeArgmax || MODE == kModeKey) {
+    const Partial r = single ? *single : reduce_member(base, p.segs, lane);
+    if (lane != 0) return;
+    if constexpr (MODE == kModeArgmax) {
+      decode_partial(r, IS64, &p.out_idx[group], &p.out_status[group]);
+    } else {
+      unsigned long long key = 0ull;
+      if (r.flags & kFlagAny) key = (r.ord << 32) | (unsigned long long)(0xFFFFFFFFu - r.idx);
+      p.out_key[group] = key;
     }
-  }
-  __syncthreads();
-  if (threadIdx.x != 0) return;
-
-  if constexpr (MODE == kModeArgmax) {
-    decode_partial(res[0], IS64, &p.out_idx[group], &p.out_status[group]);
-  } else if constexpr (MODE == kModeKey) {
-    const Partial& r = res[0];
-    unsigned long long key = 0ull;
-    if (r.flags & kFlagAny) key = (r.ord << 32) | (unsigned long long)(0xFFFFFFFFu - r.idx);
-    p.out_key[group] = key;
   } else {
+    // speculative verify: members in position order; the first row that differs from
+    // its draft (or carries a status) decides. Every member is reduced even after the
+    // decision, so that all partials are zeroed.
     const int G = P - 1;
     int32_t acc = G, corr = -1;
     uint32_t st = 0u;
     bool decided = false;
-    for (int i = 0; i < G && !decided; ++i) {
+    for (int i = 0; i < P; ++i) {
+      const Partial r = single ? *single : reduce_member(base + (int64_t)i * p.segs, p.segs, lane);
+      if (decided) continue;
       int32_t sel;
       uint32_t rs;
-      decode_partial(res[i], IS64, &sel, &rs);
-      if (rs) {
-        acc = i;
-        st = rs;
-        decided = true;
-      } else if (sel != p.drafts[group * p.draft_stride + i]) {
-        acc = i;
-        corr = sel;
-        decided = true;
+      decode_partial(r, IS64, &sel, &rs);
+      if (i < G) {
+        if (rs) {
+          acc = i;
+          st = rs;
+          decided = true;
+        } else if (sel != __ldg(p.drafts + group * p.draft_stride + i)) {
+          acc = i;
+          corr = sel;
+          decided = true;
+        }
+      } else if (p.bonus) {
+        if (rs) {
+          st = rs;
+        } else {
+          corr = sel;
+        }
       }
     }
-    if (!decided && p.bonus) {
-      int32_t sel;
-      uint32_t rs;
-      decode_partial(res[G], IS64, &sel, &rs);
-      if (rs) {
-        st = rs;
-      } else {
-        corr = sel;
-      }
+    if (lane == 0) {
+      p.accept_len[group] = acc;
+      p.correction[group] = corr;
+      p.out_status[group] = st;
     }
-    p.accept_len[group] = acc;
-    p.correction[group] = corr;
-    p.out_status[group] = st;
   }
+}
+
+// Release the warp's partial and take a ticket; true for the warp that completes a group.
+__device__ __forceinline__ bool take_ticket(Partial* slot, const Partial& part, uint32_t* counter,
+                                            uint32_t total, int lane) {
+  uint32_t t = 0u;
+  if (lane == 0) {
+    st_partial(slot, part);
+    // release this warp's partial and draw a ticket in one acq_rel atomic
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                 : "=r"(t) : "l"(counter) : "memory");
+  }
+  t = __shfl_sync(kFull, t, 0);
+  const bool last = (t == total - 1u);
+  if (last) {
+    // every lane of the finishing warp reads partials released by other warps
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    if (lane == 0) *counter = 0u;  // ready for the next call
+  }
+  return last;
 }
 
 template <int DT, bool FAST, int MODE, int THREADS, int UNROLL>
 __global__ void __launch_bounds__(THREADS)
     masked_select_kernel(const ScanParams p) {
-  __shared__ unsigned long long scratch64[33];
-  __shared__ Partial res[(MODE == kModeVerify) ? kMaxPerGroup : 1];
-  __shared__ int s_last;
-  uint32_t* scratch32 = reinterpret_cast<uint32_t*>(scratch64);
-
-  const int64_t blk = blockIdx.x;
-  const int64_t row = blk / p.segs;
-  const int seg = (int)(blk - row * p.segs);
-  const int64_t group = row / p.per_group;
-  const int64_t member = row - group * p.per_group;
+  const int lane = threadIdx.x & 31;
+  const int64_t gwarp = (int64_t)blockIdx.x * (THREADS / 32) + (threadIdx.x >> 5);
 
   // Programmatic dependent launch: everything this kernel reads may come from the
   // preceding kernel in the stream.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+#if ONYX_PDL_EARLY
+  asm volatile("griddepcontrol.launch_dependents;" :::);
+#endif
+  if (gwarp >= p.rows * p.segs) return;  // whole warps only: the lanes stay converged
+
+  const int64_t row = gwarp / p.segs;
+  const int seg = (int)(gwarp - row * p.segs);
+  const int64_t group = row / p.per_group;
+  const int64_t member = row - group * p.per_group;
 
   using St = typename Elem<DT>::storage;
   const St* row_base = static_cast<const St*>(p.logits) + group * p.group_stride +
@@ -500,33 +533,25 @@ __global__ void __launch_bounds__(THREADS)
     part = empty_partial();
     part.flags = kFlagBadState;
   } else if constexpr (FAST) {
-    part = scan_segment_fast<DT, THREADS, UNROLL>(row_base, mrow, e0, e1, scratch32);
+    part = scan_warp_fast<DT, UNROLL>(row_base, mrow, e0, e1, lane);
   } else {
-    part = scan_segment_generic<DT, THREADS>(row_base, mrow, e0, e1, scratch64);
+    part = scan_warp_generic<DT>(row_base, mrow, e0, e1, lane);
   }
   if (part.idx != 0xFFFFFFFFu) part.idx += (uint32_t)p.idx_offset;
 
+#if !ONYX_PDL_EARLY
   // let the next kernel in the stream start its prologue
   asm volatile("griddepcontrol.launch_dependents;" :::);
+#endif
 
-  const int total = p.per_group * p.segs;
-  if (total == 1) {
-    finalize_group<MODE, DT == kF64>(p, group, &part, res);
+  const uint32_t total = (uint32_t)(p.per_group * p.segs);
+  if (total == 1u) {
+    finalize_group<MODE, DT == kF64>(p, group, &part, lane);
     return;
   }
-  if (threadIdx.x == 0) {
-    st_partial(p.ws_part + blk, part);
-    __threadfence();
-    const uint32_t t = atomicAdd(p.ws_count + group, 1u);
-    s_last = (t == (uint32_t)(total - 1));
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  finalize_group<MODE, DT == kF64>(p, group, nullptr, res);
-  if (threadIdx.x == 0) p.ws_count[group] = 0u;  // ready for the next call
+  if (take_ticket(p.ws_part + gwarp, part, p.ws_count + group, total, lane))
+    finalize_group<MODE, DT == kF64>(p, group, nullptr, lane);
 }
-
 // ---------------------------------------------------------------------------------------
 // mask apply: out = allowed values bit-for-bit, -inf elsewhere; per-row status for the
 // reference's rejections (empty support, all -inf support; torch_grammar_mask.py:182-185)
@@ -690,9 +715,16 @@ __global__ void combine_keys_kernel(const unsigned long long* keys, int64_t n_pa
 // ---------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------
-constexpr int kThreads = 256;
-constexpr int kUnroll = 8;
-constexpr int kGenericPerThread = 16;
+#ifndef ONYX_THREADS
+#define ONYX_THREADS 256
+#endif
+#ifndef ONYX_UNROLL
+#define ONYX_UNROLL 8
+#endif
+constexpr int kThreads = ONYX_THREADS;
+constexpr int kUnroll = ONYX_UNROLL;
+constexpr int kWarpsPerBlock = kThreads / 32;
+constexpr int kGenericPerLane = 32;  // generic path: 1,024 elements per warp segment
 
 static thread_local int g_last_cuda_error = 0;
 
@@ -707,8 +739,8 @@ static int vec_elems(int dt) { return dt == kF32 ? 4 : 8; }
 static Plan make_plan(int dt, int64_t vocab, bool aligned) {
   Plan pl;
   pl.fast = aligned && (dt == kF32 || dt == kF16 || dt == kBF16);
-  pl.seg_elems = pl.fast ? (int64_t)kThreads * kUnroll * vec_elems(dt)
-                         : (int64_t)kThreads * kGenericPerThread;
+  // one segment per warp
+  pl.seg_elems = pl.fast ? (int64_t)32 * kUnroll * vec_elems(dt) : (int64_t)32 * kGenericPerLane;
   pl.segs = (int)((vocab + pl.seg_elems - 1) / pl.seg_elems);
   return pl;
 }
@@ -723,7 +755,7 @@ static size_t workspace_bytes_for(int64_t rows, int64_t groups, const Plan& pl, 
 
 template <int DT, bool FAST, int MODE>
 static cudaError_t launch_t(const ScanParams& p, cudaStream_t stream, bool pdl) {
-  const int64_t blocks = p.rows * p.segs;
+  const int64_t blocks = (p.rows * p.segs + kWarpsPerBlock - 1) / kWarpsPerBlock;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)blocks, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
