@@ -52,6 +52,7 @@ extern "C" {
 #define ONYX_ERR_UNSUPPORTED_DTYPE 2
 #define ONYX_ERR_WORKSPACE 3
 #define ONYX_ERR_CUDA 4
+#define ONYX_ERR_SCRATCH_LIMIT 5 /* onyx_masked_argmax_noalloc: beyond its fixed scratch */
 
 /* per-row status bits */
 #define ONYX_STATUS_EMPTY_MASK 1u     /* no valid token: grammar no-decision
@@ -145,6 +146,31 @@ ONYX_API int onyx_vocab_partial_argmax(const void* logits, int dtype, int64_t ro
 /* step 2: keys[part*rows + r] for n_parts shards -> out_idx / out_status as masked argmax */
 ONYX_API int onyx_combine_partials(const uint64_t* keys, int64_t n_parts, int64_t rows, int32_t* out_idx,
                           uint32_t* out_status, void* stream);
+
+/*
+ * Allocation-free masked greedy selection. No counterpart in the reference: it is the
+ * onyx_masked_argmax contract for callers that cannot allocate device memory when they
+ * call -- a serving process whose GPU memory is reserved up front by its own pool, a
+ * foreign-language binding that only receives pointers to buffers allocated elsewhere, or
+ * code where an allocation would synchronise or fail -- and so cannot pass a workspace.
+ * The caller passes only inputs and outputs (same meaning as onyx_masked_argmax).
+ *
+ * The partials and tickets of rows split over several warps live in a fixed scratch array
+ * compiled into the library: onyx_noalloc_scratch_bytes() bytes (1 MiB) held on every GPU
+ * that loads the library until the process exits. A request needing more than that
+ * (about rows * ceil(vocab / 2048) * 16 bytes for 16-bit rows) returns
+ * ONYX_ERR_SCRATCH_LIMIT without launching anything. The call allocates nothing: the first
+ * call on each device looks up the scratch address (cudaGetSymbolAddress, on the current
+ * device), so make that first call before any stream capture; every call clears the
+ * tickets it uses with cudaMemsetAsync on `stream`. All calls on a device share the one
+ * array, so calls that can overlap on the GPU (other streams or host threads) race and
+ * must be serialised by the caller.
+ */
+ONYX_API size_t onyx_noalloc_scratch_bytes(void);
+ONYX_API int onyx_masked_argmax_noalloc(const void* logits, int dtype, int64_t rows,
+                                        int64_t vocab, int64_t row_stride, const uint32_t* mask,
+                                        int64_t mask_stride, int32_t* out_idx,
+                                        uint32_t* out_status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -28,6 +28,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <mutex>
 
 #ifndef ONYX_PDL_EARLY
 #define ONYX_PDL_EARLY 0
@@ -842,6 +843,9 @@ const char* onyx_error_string(int code) {
     case ONYX_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype";
     case ONYX_ERR_WORKSPACE: return "workspace missing, too small or not 256-byte aligned";
     case ONYX_ERR_CUDA: return "CUDA launch failed (see onyx_last_cuda_error)";
+    case ONYX_ERR_SCRATCH_LIMIT:
+      return "request needs more than the library's fixed no-alloc scratch "
+             "(onyx_noalloc_scratch_bytes); use onyx_masked_argmax with a workspace";
   }
   return "unknown error";
 }
@@ -1110,3 +1114,106 @@ int onyx_combine_partials(const uint64_t* keys, int64_t n_parts, int64_t rows, i
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free variant of onyx_masked_argmax.
+//
+// Who needs it: callers that cannot allocate device memory at the point of the call and
+// so cannot hand over a workspace -- e.g. a serving process whose device memory was
+// reserved up front by its own pool, a host-language binding that only ever receives
+// pointers to buffers someone else allocated, or code running where an allocation would
+// synchronise or fail. This entry point takes only inputs and outputs; the split-row
+// partials and tickets live in a fixed scratch array compiled into the library.
+//
+// The array is a file-scope __device__ symbol, so every GPU that loads this library holds
+// kNoAllocScratchBytes of it until the process exits. Host code cannot use the symbol's
+// name as a device address; the address is looked up once per device with
+// cudaGetSymbolAddress, with that device current, on the first call made on that device.
+// That first call should therefore happen before any stream capture. Every call on a
+// device shares the one array: calls whose kernels may overlap on the GPU (different
+// streams, or different host threads) race and must be serialised by the caller.
+// ---------------------------------------------------------------------------------------
+namespace onyx {
+
+constexpr size_t kNoAllocScratchBytes = 1u << 20;  // 1 MiB per device
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_noalloc_mutex;
+static void* g_noalloc_address[kNoAllocMaxDevices] = {};
+
+// Device address of this device's scratch array (looked up on first use).
+static int noalloc_scratch_address(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    g_last_cuda_error = (int)e;
+    return ONYX_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return ONYX_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_address[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || ptr == nullptr) {
+      g_last_cuda_error = (int)(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+      return ONYX_ERR_CUDA;
+    }
+    g_noalloc_address[dev] = ptr;
+  }
+  *out = g_noalloc_address[dev];
+  return ONYX_OK;
+}
+
+}  // namespace onyx
+
+extern "C" size_t onyx_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+extern "C" int onyx_masked_argmax_noalloc(const void* logits, int dtype, int64_t rows,
+                                          int64_t vocab, int64_t row_stride,
+                                          const uint32_t* mask, int64_t mask_stride,
+                                          int32_t* out_idx, uint32_t* out_status,
+                                          void* stream) {
+  int rc = common_checks(logits, dtype, rows, vocab, row_stride);
+  if (rc) return rc;
+  if (rows == 0) return ONYX_OK;
+  if (!out_idx || !out_status) return ONYX_ERR_INVALID_ARGUMENT;
+  if (mask && mask_stride < (vocab + 31) / 32 && rows > 1) return ONYX_ERR_INVALID_ARGUMENT;
+  const int es = dtype_bytes(dtype);
+  const bool aligned = aligned16(logits) && ((row_stride * es) % 16 == 0 || rows == 1);
+  const Plan pl = make_plan(dtype, vocab, aligned);
+  // scratch layout: ticket counters [rows] first, then partials [rows * segs]
+  const size_t count_bytes = align_up((size_t)rows * sizeof(uint32_t), 256);
+  const size_t part_bytes = (size_t)rows * pl.segs * sizeof(Partial);
+  const bool split = pl.segs > 1;
+  if (split && count_bytes + part_bytes > kNoAllocScratchBytes) return ONYX_ERR_SCRATCH_LIMIT;
+  ScanParams p = {};
+  p.logits = logits;
+  p.group_stride = row_stride;
+  p.vocab = vocab;
+  p.mask = mask;
+  p.mask_group_stride = mask_stride;
+  p.rows = rows;
+  p.per_group = 1;
+  p.segs = pl.segs;
+  p.seg_elems = pl.seg_elems;
+  p.out_idx = out_idx;
+  p.out_status = out_status;
+  if (split) {
+    void* base = nullptr;
+    rc = noalloc_scratch_address(&base);
+    if (rc) return rc;
+    p.ws_count = static_cast<uint32_t*>(base);
+    p.ws_part = reinterpret_cast<Partial*>(static_cast<char*>(base) + count_bytes);
+    // the tickets must start at zero whatever an earlier call left behind
+    const cudaError_t e =
+        cudaMemsetAsync(p.ws_count, 0, (size_t)rows * sizeof(uint32_t), (cudaStream_t)stream);
+    if (e != cudaSuccess) {
+      g_last_cuda_error = (int)e;
+      return ONYX_ERR_CUDA;
+    }
+  }
+  return finish_launch(
+      dispatch<kModeArgmax>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled()));
+}
