@@ -54,6 +54,9 @@ extern "C" {
 #define ONYX_ERR_CUDA 4
 #define ONYX_ERR_SCRATCH_LIMIT 5 /* onyx_masked_argmax_noalloc: beyond its fixed scratch */
 
+/* size of the per-device scratch array of onyx_masked_argmax_noalloc */
+#define ONYX_NOALLOC_SCRATCH_BYTES (1u << 20)
+
 /* per-row status bits */
 #define ONYX_STATUS_EMPTY_MASK 1u     /* no valid token: grammar no-decision
                                          (grammar_selection.py:122-127) */
@@ -155,18 +158,17 @@ ONYX_API int onyx_combine_partials(const uint64_t* keys, int64_t n_parts, int64_
  * code where an allocation would synchronise or fail -- and so cannot pass a workspace.
  * The caller passes only inputs and outputs (same meaning as onyx_masked_argmax).
  *
- * The partials and tickets of rows split over several warps live in a fixed scratch array
- * compiled into the library: onyx_noalloc_scratch_bytes() bytes (1 MiB) held on every GPU
- * that loads the library until the process exits. A request needing more than that
- * (about rows * ceil(vocab / 2048) * 16 bytes for 16-bit rows) returns
- * ONYX_ERR_SCRATCH_LIMIT without launching anything. The call allocates nothing: the first
+ * The partials and tickets of rows split over several CTAs live in a fixed scratch array
+ * compiled into the library: ONYX_NOALLOC_SCRATCH_BYTES (1 MiB) held on every GPU that
+ * loads the library until the process exits. A request needing more than that --
+ * 4 bytes per row plus 16 bytes per row per 16,384 16-bit (8,192 f32) columns, rounded
+ * up -- returns ONYX_ERR_SCRATCH_LIMIT without launching anything. The call allocates nothing: the first
  * call on each device looks up the scratch address (cudaGetSymbolAddress, on the current
  * device), so make that first call before any stream capture; every call clears the
  * tickets it uses with cudaMemsetAsync on `stream`. All calls on a device share the one
  * array, so calls that can overlap on the GPU (other streams or host threads) race and
  * must be serialised by the caller.
  */
-ONYX_API size_t onyx_noalloc_scratch_bytes(void);
 ONYX_API int onyx_masked_argmax_noalloc(const void* logits, int dtype, int64_t rows,
                                         int64_t vocab, int64_t row_stride, const uint32_t* mask,
                                         int64_t mask_stride, int32_t* out_idx,

@@ -24,6 +24,7 @@ ERR_UNSUPPORTED_DTYPE = 2
 ERR_WORKSPACE = 3
 ERR_CUDA = 4
 ERR_SCRATCH_LIMIT = 5
+NOALLOC_SCRATCH_BYTES = 1 << 20
 
 STATUS_EMPTY_MASK = 1
 STATUS_ALL_NEG_INF = 2
@@ -53,7 +54,6 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "onyx_vocab_partial_argmax": (
         _i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _sz, _vp]),
     "onyx_combine_partials": (_i32, [_vp, _i64, _i64, _vp, _vp, _vp]),
-    "onyx_noalloc_scratch_bytes": (_sz, []),
     "onyx_masked_argmax_noalloc": (
         _i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
 }

@@ -51,9 +51,10 @@ struct ScanParams {
   int64_t idx_offset;  // global index of column 0 (vocabulary shards)
   int64_t rows;        // total rows = groups * per_group
   int per_group;       // rows per group (gamma + 1 for verify, else 1)
-  int segs;            // segments per row
-  int64_t seg_elems;   // elements per segment (multiple of 32)
-  Partial* ws_part;    // [rows * segs]
+  int segs;            // warp segments per row
+  int ctas_per_row;    // CTAs per row (each covers blockDim/32 consecutive segments)
+  int64_t seg_elems;   // elements per warp segment (multiple of 32)
+  Partial* ws_part;    // [rows * ctas_per_row], one partial per CTA
   uint32_t* ws_count;  // [groups]
   // outputs
   int32_t* out_idx;
@@ -193,10 +194,12 @@ __device__ __forceinline__ Partial scan_warp_fast(const void* row_base, const ui
   // phase 1: masked maximum, no indices; each vector's own maximum is kept for phase 2
   uint32_t bits[UNROLL];
   uint32_t any = tail_bit;
+  // segment starts and vector strides are multiples of 32 elements, so a lane's bits
+  // always sit at the same offset in their mask word
+  const uint32_t lane_shift = (uint32_t)(lane * E) & 31u;
 #pragma unroll
   for (int k = 0; k < UNROLL; ++k) {
-    const int64_t e = e0 + ((int64_t)k * 32 + lane) * E;
-    bits[k] = (w[k] >> (e & 31)) & kLaneBits;
+    bits[k] = (w[k] >> lane_shift) & kLaneBits;
     any |= bits[k];
   }
   float tmax;
@@ -229,61 +232,64 @@ __device__ __forceinline__ Partial scan_warp_fast(const void* row_base, const ui
   part.idx = 0xFFFFFFFFu;
   if (M == 0u || M == kOrd32NaN) return part;
 
-  // phase 2 (only lanes holding the maximum): the first vector whose maximum equals M
+  // phase 2, warp-wide: the lowest (vector k, lane) whose kept vector maximum equals M
   // (a vector with valid elements reaches M only through a valid element equal to M),
-  // then the first valid element of that vector equal to M. Equality is float equality,
-  // so -0.0 and +0.0 match alike.
-  uint32_t cand = 0xFFFFFFFFu;
-  if (tord == M) {
-    const float mf = __uint_as_float((M & 0x80000000u) ? (M & 0x7FFFFFFFu) : ~M);
-    int kk = -1;
-    uint4 xv = make_uint4(0u, 0u, 0u, 0u);
-    uint32_t bv = 0u;
-    if constexpr (DT == kF32) {
+  // then the lowest valid element of that vector equal to M. Element order within the
+  // segment is (k, lane, j), so this is the lowest index. Equality is float equality:
+  // -0.0 and +0.0 match alike.
+  const float mf = __uint_as_float((M & 0x80000000u) ? (M & 0x7FFFFFFFu) : ~M);
+  uint32_t key = 0xFFFFFFFFu;
+  uint32_t m2 = 0u;
+  if constexpr (DT == kF32) {
 #pragma unroll
-      for (int k = UNROLL - 1; k >= 0; --k) {
-        if (bits[k] && __uint_as_float(vmax[k]) == mf) {
-          kk = k;
-          xv = x[k];
-          bv = bits[k];
-        }
-      }
-      if (kk >= 0) {
-        int j = 3;
-        if ((bv & 4u) && __uint_as_float(xv.z) == mf) j = 2;
-        if ((bv & 2u) && __uint_as_float(xv.y) == mf) j = 1;
-        if ((bv & 1u) && __uint_as_float(xv.x) == mf) j = 0;
-        cand = (uint32_t)(e0 + ((int64_t)kk * 32 + lane) * E + j);
-      }
-    } else {
-      const uint32_t h = V::from_f32(mf);
-      const uint32_t m2 = h | (h << 16);
+    for (int k = UNROLL - 1; k >= 0; --k)
+      if (bits[k] && __uint_as_float(vmax[k]) == mf) key = ((uint32_t)k << 5) | lane;
+  } else {
+    const uint32_t h = V::from_f32(mf);
+    m2 = h | (h << 16);
 #pragma unroll
-      for (int k = UNROLL - 1; k >= 0; --k) {
-        if (bits[k] && V::eq_mask(vmax[k], m2)) {
-          kk = k;
-          xv = x[k];
-          bv = bits[k];
-        }
-      }
-      if (kk >= 0) {
-        uint32_t m01, m23, m45, m67;
-        expand4_16(bv, m01, m23);
-        expand4_16(bv >> 4, m45, m67);
-        // element j of the vector owns 16-bit lane j of the 64-bit words q (j < 4), r
-        const uint32_t q0 = V::eq_mask(xv.x, m2) & m01;
-        const uint32_t q1 = V::eq_mask(xv.y, m2) & m23;
-        const uint32_t q2 = V::eq_mask(xv.z, m2) & m45;
-        const uint32_t q3 = V::eq_mask(xv.w, m2) & m67;
-        const unsigned long long q = (unsigned long long)(q0 | ((unsigned long long)q1 << 32));
-        const unsigned long long r = (unsigned long long)(q2 | ((unsigned long long)q3 << 32));
-        const int j = q ? (__ffsll((long long)q) - 1) / 16 : 4 + (__ffsll((long long)r) - 1) / 16;
-        cand = (uint32_t)(e0 + ((int64_t)kk * 32 + lane) * E + j);
-      }
-    }
-    if (kk < 0 && tail_bit && ord32(V::scalar(tail_raw)) == M) cand = (uint32_t)tail_e;
+    for (int k = UNROLL - 1; k >= 0; --k)
+      if (bits[k] && V::eq_mask(vmax[k], m2)) key = ((uint32_t)k << 5) | lane;
   }
-  part.idx = __reduce_min_sync(kFull, cand);
+  if (key == 0xFFFFFFFFu && tail_bit && ord32(V::scalar(tail_raw)) == M)
+    key = ((uint32_t)UNROLL << 5) | lane;  // the ragged tail follows every full vector
+  const uint32_t win = __reduce_min_sync(kFull, key);
+  const int wk = (int)(win >> 5), wl = (int)(win & 31u);
+  uint32_t cand;
+  if (wk >= UNROLL) {
+    cand = (uint32_t)(e0 + nv * E + wl);
+  } else {
+    uint4 xv = x[0];
+    uint32_t bv = bits[0];
+#pragma unroll
+    for (int k = 1; k < UNROLL; ++k)
+      if (k == wk) {  // warp-uniform
+        xv = x[k];
+        bv = bits[k];
+      }
+    int j;
+    if constexpr (DT == kF32) {
+      j = 3;
+      if ((bv & 4u) && __uint_as_float(xv.z) == mf) j = 2;
+      if ((bv & 2u) && __uint_as_float(xv.y) == mf) j = 1;
+      if ((bv & 1u) && __uint_as_float(xv.x) == mf) j = 0;
+    } else {
+      uint32_t m01, m23, m45, m67;
+      expand4_16(bv, m01, m23);
+      expand4_16(bv >> 4, m45, m67);
+      // element j of the vector owns 16-bit lane j of the 64-bit words q (j < 4), r
+      const uint32_t q0 = V::eq_mask(xv.x, m2) & m01;
+      const uint32_t q1 = V::eq_mask(xv.y, m2) & m23;
+      const uint32_t q2 = V::eq_mask(xv.z, m2) & m45;
+      const uint32_t q3 = V::eq_mask(xv.w, m2) & m67;
+      const unsigned long long q = (unsigned long long)q0 | ((unsigned long long)q1 << 32);
+      const unsigned long long r = (unsigned long long)q2 | ((unsigned long long)q3 << 32);
+      j = q ? (__ffsll((long long)q) - 1) >> 4 : 4 + ((__ffsll((long long)r) - 1) >> 4);
+    }
+    j = __shfl_sync(kFull, j, wl);
+    cand = (uint32_t)(e0 + ((int64_t)wk * 32 + wl) * E + j);
+  }
+  part.idx = cand;
   return part;
 }
 
@@ -422,9 +428,9 @@ template <int MODE, bool IS64>
 __device__ void finalize_group(const ScanParams& p, int64_t group, const Partial* single,
                                int lane) {
   const int P = p.per_group;
-  Partial* base = single ? nullptr : p.ws_part + group * (int64_t)P * p.segs;
+  Partial* base = single ? nullptr : p.ws_part + group * (int64_t)P * p.ctas_per_row;
   if constexpr (MODE == kModeArgmax || MODE == kModeKey) {
-    const Partial r = single ? *single : reduce_member(base, p.segs, lane);
+    const Partial r = single ? *single : reduce_member(base, p.ctas_per_row, lane);
     if (lane != 0) return;
     if constexpr (MODE == kModeArgmax) {
       decode_partial(r, IS64, &p.out_idx[group], &p.out_status[group]);
@@ -442,7 +448,8 @@ __device__ void finalize_group(const ScanParams& p, int64_t group, const Partial
     uint32_t st = 0u;
     bool decided = false;
     for (int i = 0; i < P; ++i) {
-      const Partial r = single ? *single : reduce_member(base + (int64_t)i * p.segs, p.segs, lane);
+      const Partial r =
+          single ? *single : reduce_member(base + (int64_t)i * p.ctas_per_row, p.ctas_per_row, lane);
       if (decided) continue;
       int32_t sel;
       uint32_t rs;
@@ -493,11 +500,18 @@ __device__ __forceinline__ bool take_ticket(Partial* slot, const Partial& part, 
   return last;
 }
 
-template <int DT, bool FAST, int MODE, int THREADS, int UNROLL>
-__global__ void __launch_bounds__(THREADS)
+template <int DT, bool FAST, int MODE, int MAXWARPS, int UNROLL>
+__global__ void __launch_bounds__(MAXWARPS * 32)
     masked_select_kernel(const ScanParams p) {
+  __shared__ Partial s_part[MAXWARPS];
   const int lane = threadIdx.x & 31;
-  const int64_t gwarp = (int64_t)blockIdx.x * (THREADS / 32) + (threadIdx.x >> 5);
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int64_t row = blockIdx.x / p.ctas_per_row;
+  const int cta = (int)(blockIdx.x - row * p.ctas_per_row);
+  const int seg = cta * nwarps + warp;
+  const int64_t group = row / p.per_group;
+  const int64_t member = row - group * p.per_group;
 
   // Programmatic dependent launch: everything this kernel reads may come from the
   // preceding kernel in the stream.
@@ -505,12 +519,6 @@ __global__ void __launch_bounds__(THREADS)
 #if ONYX_PDL_EARLY
   asm volatile("griddepcontrol.launch_dependents;" :::);
 #endif
-  if (gwarp >= p.rows * p.segs) return;  // whole warps only: the lanes stay converged
-
-  const int64_t row = gwarp / p.segs;
-  const int seg = (int)(gwarp - row * p.segs);
-  const int64_t group = row / p.per_group;
-  const int64_t member = row - group * p.per_group;
 
   using St = typename Elem<DT>::storage;
   const St* row_base = static_cast<const St*>(p.logits) + group * p.group_stride +
@@ -526,33 +534,43 @@ __global__ void __launch_bounds__(THREADS)
       mrow = p.mask + group * p.mask_group_stride + member * p.mask_row_stride;
     }
   }
-  const int64_t e0 = (int64_t)seg * p.seg_elems;
-  const int64_t e1 = min(e0 + p.seg_elems, p.vocab);
 
-  Partial part;
+  Partial part = empty_partial();
   if (bad_state) {
-    part = empty_partial();
     part.flags = kFlagBadState;
-  } else if constexpr (FAST) {
-    part = scan_warp_fast<DT, UNROLL>(row_base, mrow, e0, e1, lane);
-  } else {
-    part = scan_warp_generic<DT>(row_base, mrow, e0, e1, lane);
+  } else if (seg < p.segs) {  // warp-uniform
+    const int64_t e0 = (int64_t)seg * p.seg_elems;
+    const int64_t e1 = min(e0 + p.seg_elems, p.vocab);
+    if constexpr (FAST) {
+      part = scan_warp_fast<DT, UNROLL>(row_base, mrow, e0, e1, lane);
+    } else {
+      part = scan_warp_generic<DT>(row_base, mrow, e0, e1, lane);
+    }
+    if (part.idx != 0xFFFFFFFFu) part.idx += (uint32_t)p.idx_offset;
   }
-  if (part.idx != 0xFFFFFFFFu) part.idx += (uint32_t)p.idx_offset;
 
 #if !ONYX_PDL_EARLY
   // let the next kernel in the stream start its prologue
   asm volatile("griddepcontrol.launch_dependents;" :::);
 #endif
 
-  const uint32_t total = (uint32_t)(p.per_group * p.segs);
+  // merge the CTA's warp partials in shared memory; warp 0 carries the result on
+  if (nwarps > 1) {
+    if (lane == 0) s_part[warp] = part;
+    __syncthreads();
+    if (warp != 0) return;
+    part = warp_merge(lane < nwarps ? s_part[lane] : empty_partial());
+  }
+
+  const uint32_t total = (uint32_t)(p.per_group * p.ctas_per_row);
   if (total == 1u) {
     finalize_group<MODE, DT == kF64>(p, group, &part, lane);
     return;
   }
-  if (take_ticket(p.ws_part + gwarp, part, p.ws_count + group, total, lane))
+  if (take_ticket(p.ws_part + blockIdx.x, part, p.ws_count + group, total, lane))
     finalize_group<MODE, DT == kF64>(p, group, nullptr, lane);
 }
+
 // ---------------------------------------------------------------------------------------
 // mask apply: out = allowed values bit-for-bit, -inf elsewhere; per-row status for the
 // reference's rejections (empty support, all -inf support; torch_grammar_mask.py:182-185)
@@ -732,7 +750,9 @@ static thread_local int g_last_cuda_error = 0;
 struct Plan {
   bool fast;
   int64_t seg_elems;
-  int segs;
+  int segs;          // warp segments per row
+  int warps;         // warps per CTA
+  int ctas_per_row;  // CTAs per row
 };
 
 static int vec_elems(int dt) { return dt == kF32 ? 4 : 8; }
@@ -743,23 +763,26 @@ static Plan make_plan(int dt, int64_t vocab, bool aligned) {
   // one segment per warp
   pl.seg_elems = pl.fast ? (int64_t)32 * kUnroll * vec_elems(dt) : (int64_t)32 * kGenericPerLane;
   pl.segs = (int)((vocab + pl.seg_elems - 1) / pl.seg_elems);
+  pl.warps = pl.segs < kWarpsPerBlock ? pl.segs : kWarpsPerBlock;
+  pl.ctas_per_row = (pl.segs + pl.warps - 1) / pl.warps;
   return pl;
 }
 
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 static size_t workspace_bytes_for(int64_t rows, int64_t groups, const Plan& pl, int per_group) {
-  if ((int64_t)pl.segs * per_group == 1) return 0;
-  return align_up((size_t)rows * pl.segs * sizeof(Partial), 256) +
+  if ((int64_t)pl.ctas_per_row * per_group == 1) return 0;
+  return align_up((size_t)rows * pl.ctas_per_row * sizeof(Partial), 256) +
          align_up((size_t)groups * sizeof(uint32_t), 256);
 }
 
 template <int DT, bool FAST, int MODE>
 static cudaError_t launch_t(const ScanParams& p, cudaStream_t stream, bool pdl) {
-  const int64_t blocks = (p.rows * p.segs + kWarpsPerBlock - 1) / kWarpsPerBlock;
+  const int64_t blocks = p.rows * p.ctas_per_row;
+  const int warps = (p.segs + p.ctas_per_row - 1) / p.ctas_per_row;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)blocks, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3((unsigned)(32 * warps), 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -767,7 +790,7 @@ static cudaError_t launch_t(const ScanParams& p, cudaStream_t stream, bool pdl) 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, masked_select_kernel<DT, FAST, MODE, kThreads, kUnroll>, p);
+  return cudaLaunchKernelEx(&cfg, masked_select_kernel<DT, FAST, MODE, kWarpsPerBlock, kUnroll>, p);
 }
 
 template <int MODE>
@@ -817,7 +840,7 @@ static int bind_workspace(ScanParams& p, void* ws, size_t ws_bytes, size_t need,
     return ONYX_OK;
   }
   if (!ws || ws_bytes < need || ((uintptr_t)ws & 255u)) return ONYX_ERR_WORKSPACE;
-  const size_t part_bytes = align_up((size_t)p.rows * p.segs * sizeof(Partial), 256);
+  const size_t part_bytes = align_up((size_t)p.rows * p.ctas_per_row * sizeof(Partial), 256);
   p.ws_part = static_cast<Partial*>(ws);
   p.ws_count = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + part_bytes);
   (void)groups;
@@ -845,7 +868,7 @@ const char* onyx_error_string(int code) {
     case ONYX_ERR_CUDA: return "CUDA launch failed (see onyx_last_cuda_error)";
     case ONYX_ERR_SCRATCH_LIMIT:
       return "request needs more than the library's fixed no-alloc scratch "
-             "(onyx_noalloc_scratch_bytes); use onyx_masked_argmax with a workspace";
+             "(ONYX_NOALLOC_SCRATCH_BYTES); use onyx_masked_argmax with a workspace";
   }
   return "unknown error";
 }
@@ -897,6 +920,7 @@ int onyx_masked_argmax(const void* logits, int dtype, int64_t rows, int64_t voca
   p.rows = rows;
   p.per_group = 1;
   p.segs = pl.segs;
+  p.ctas_per_row = pl.ctas_per_row;
   p.seg_elems = pl.seg_elems;
   p.out_idx = out_idx;
   p.out_status = out_status;
@@ -930,6 +954,7 @@ int onyx_gather_masked_argmax(const void* logits, int dtype, int64_t rows, int64
   p.rows = rows;
   p.per_group = 1;
   p.segs = pl.segs;
+  p.ctas_per_row = pl.ctas_per_row;
   p.seg_elems = pl.seg_elems;
   p.out_idx = out_idx;
   p.out_status = out_status;
@@ -971,6 +996,7 @@ int onyx_spec_verify(const void* logits, int dtype, int64_t batch, int64_t gamma
   p.rows = batch * P;
   p.per_group = P;
   p.segs = pl.segs;
+  p.ctas_per_row = pl.ctas_per_row;
   p.seg_elems = pl.seg_elems;
   p.out_status = out_status;
   p.drafts = drafts;
@@ -1014,6 +1040,7 @@ int onyx_vocab_partial_argmax(const void* logits, int dtype, int64_t rows, int64
   p.rows = rows;
   p.per_group = 1;
   p.segs = pl.segs;
+  p.ctas_per_row = pl.ctas_per_row;
   p.seg_elems = pl.seg_elems;
   p.out_key = reinterpret_cast<unsigned long long*>(out_keys);
   rc = bind_workspace(p, workspace, workspace_bytes, workspace_bytes_for(rows, rows, pl, 1), rows);
@@ -1135,7 +1162,7 @@ int onyx_combine_partials(const uint64_t* keys, int64_t n_parts, int64_t rows, i
 // ---------------------------------------------------------------------------------------
 namespace onyx {
 
-constexpr size_t kNoAllocScratchBytes = 1u << 20;  // 1 MiB per device
+constexpr size_t kNoAllocScratchBytes = ONYX_NOALLOC_SCRATCH_BYTES;  // 1 MiB per device
 constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
@@ -1168,8 +1195,6 @@ static int noalloc_scratch_address(void** out) {
 
 }  // namespace onyx
 
-extern "C" size_t onyx_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
-
 extern "C" int onyx_masked_argmax_noalloc(const void* logits, int dtype, int64_t rows,
                                           int64_t vocab, int64_t row_stride,
                                           const uint32_t* mask, int64_t mask_stride,
@@ -1185,8 +1210,8 @@ extern "C" int onyx_masked_argmax_noalloc(const void* logits, int dtype, int64_t
   const Plan pl = make_plan(dtype, vocab, aligned);
   // scratch layout: ticket counters [rows] first, then partials [rows * segs]
   const size_t count_bytes = align_up((size_t)rows * sizeof(uint32_t), 256);
-  const size_t part_bytes = (size_t)rows * pl.segs * sizeof(Partial);
-  const bool split = pl.segs > 1;
+  const size_t part_bytes = (size_t)rows * pl.ctas_per_row * sizeof(Partial);
+  const bool split = pl.ctas_per_row > 1;
   if (split && count_bytes + part_bytes > kNoAllocScratchBytes) return ONYX_ERR_SCRATCH_LIMIT;
   ScanParams p = {};
   p.logits = logits;
@@ -1197,6 +1222,7 @@ extern "C" int onyx_masked_argmax_noalloc(const void* logits, int dtype, int64_t
   p.rows = rows;
   p.per_group = 1;
   p.segs = pl.segs;
+  p.ctas_per_row = pl.ctas_per_row;
   p.seg_elems = pl.seg_elems;
   p.out_idx = out_idx;
   p.out_status = out_status;

@@ -11,8 +11,6 @@ run stopping at the first failure has already run every other test.
 
 from __future__ import annotations
 
-import ctypes
-
 import numpy as np
 import pytest
 import torch
@@ -77,11 +75,21 @@ def test_noalloc_unmasked_rows(cuda_lib):
 
 
 def test_noalloc_rejects_requests_beyond_its_scratch(cuda_lib):
+    """A request whose split-row partials exceed the fixed scratch is refused before any
+    launch. The buffers are real and sized for the request, so nothing could read out of
+    bounds even if the call were accepted."""
     lib = cuda_lib
-    assert lib.onyx_noalloc_scratch_bytes() == 1 << 20
-    # 1024 rows x 256,000 bf16 need ~2 MB of partials: refused before any launch
-    dummy = ctypes.c_void_p(16)
-    rc = lib.onyx_masked_argmax_noalloc(dummy, _lib.DTYPE_BF16, 1024, 256000, 256000, dummy,
-                                        8000, dummy, dummy, None)
+    rows, vocab = 32768, 16385  # 9 warp segments -> 2 CTAs per row: 32,768 * (4 + 32) B > 1 MiB
+    count_bytes = (rows * 4 + 255) // 256 * 256
+    assert count_bytes + rows * 2 * 16 > _lib.NOALLOC_SCRATCH_BYTES
+    x = torch.empty((rows, vocab), dtype=torch.bfloat16, device="cuda:0")
+    m = torch.zeros((rows, (vocab + 31) // 32), dtype=torch.int32, device="cuda:0")
+    idx = torch.empty(rows, dtype=torch.int32, device="cuda:0")
+    st = torch.empty(rows, dtype=torch.int32, device="cuda:0")
+    rc = lib.onyx_masked_argmax_noalloc(
+        x.data_ptr(), _lib.DTYPE_BF16, rows, vocab, x.stride(0), m.data_ptr(), m.stride(0),
+        idx.data_ptr(), st.data_ptr(), torch.cuda.current_stream().cuda_stream,
+    )
+    torch.cuda.synchronize()
     assert rc == _lib.ERR_SCRATCH_LIMIT
     assert b"scratch" in lib.onyx_error_string(rc)
