@@ -26,6 +26,8 @@
 #include "onyx_common.cuh"
 #include "../../include/onyx_b200.h"
 
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <cstdlib>
 #include <mutex>
@@ -571,6 +573,73 @@ __global__ void __launch_bounds__(MAXWARPS * 32)
     finalize_group<MODE, DT == kF64>(p, group, nullptr, lane);
 }
 
+// Same selection with the CTAs of one row grouped in a thread-block cluster: each CTA
+// stores its partial straight into rank 0's shared memory (distributed shared memory) and
+// one hardware cluster barrier replaces the global ticket -- no atomics, no fences, no
+// workspace. Used for the argmax / gather / shard-key modes when a row needs at most
+// kMaxClusterCtas CTAs.
+constexpr int kMaxClusterCtas = 8;
+
+template <int DT, bool FAST, int MODE, int MAXWARPS, int UNROLL>
+__global__ void __launch_bounds__(MAXWARPS * 32)
+    masked_select_cluster_kernel(const ScanParams p) {
+  static_assert(MODE != kModeVerify, "verify groups span several rows");
+  namespace cg = cooperative_groups;
+  __shared__ Partial s_part[MAXWARPS];
+  __shared__ Partial s_cta[kMaxClusterCtas];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+  const int64_t row = blockIdx.x / p.ctas_per_row;  // one cluster per row
+  const int seg = rank * nwarps + warp;
+
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  using St = typename Elem<DT>::storage;
+  const St* row_base = static_cast<const St*>(p.logits) + row * p.group_stride;
+  const uint32_t* mrow = nullptr;
+  bool bad_state = false;
+  if (p.mask) {
+    if (p.state_ids) {
+      const int32_t s = __ldg(p.state_ids + row);
+      bad_state = (s < 0) || ((int64_t)s >= p.n_states);
+      mrow = p.mask + (bad_state ? 0 : (int64_t)s * p.mask_row_stride);
+    } else {
+      mrow = p.mask + row * p.mask_group_stride;
+    }
+  }
+
+  Partial part = empty_partial();
+  if (bad_state) {
+    part.flags = kFlagBadState;
+  } else if (seg < p.segs) {  // warp-uniform
+    const int64_t e0 = (int64_t)seg * p.seg_elems;
+    const int64_t e1 = min(e0 + p.seg_elems, p.vocab);
+    if constexpr (FAST) {
+      part = scan_warp_fast<DT, UNROLL>(row_base, mrow, e0, e1, lane);
+    } else {
+      part = scan_warp_generic<DT>(row_base, mrow, e0, e1, lane);
+    }
+    if (part.idx != 0xFFFFFFFFu) part.idx += (uint32_t)p.idx_offset;
+  }
+
+  asm volatile("griddepcontrol.launch_dependents;" :::);
+
+  if (lane == 0) s_part[warp] = part;
+  __syncthreads();
+  if (warp == 0) {
+    part = warp_merge(lane < nwarps ? s_part[lane] : empty_partial());
+    if (lane == 0) *cluster.map_shared_rank(&s_cta[rank], 0) = part;
+  }
+  cluster.sync();  // every CTA's partial has landed in rank 0's shared memory
+  if (rank == 0 && warp == 0) {
+    part = warp_merge(lane < p.ctas_per_row ? s_cta[lane] : empty_partial());
+    finalize_group<MODE, DT == kF64>(p, row, &part, lane);
+  }
+}
+
 // ---------------------------------------------------------------------------------------
 // mask apply: out = allowed values bit-for-bit, -inf elsewhere; per-row status for the
 // reference's rejections (empty support, all -inf support; torch_grammar_mask.py:182-185)
@@ -793,6 +862,84 @@ static cudaError_t launch_t(const ScanParams& p, cudaStream_t stream, bool pdl) 
   return cudaLaunchKernelEx(&cfg, masked_select_kernel<DT, FAST, MODE, kWarpsPerBlock, kUnroll>, p);
 }
 
+constexpr int kMaxClusterWarps = 16;
+
+// Cluster layout for one row: at most kMaxClusterCtas CTAs of at most kMaxClusterWarps warps,
+// one warp per segment. False when the row needs more (the ticket kernel handles it).
+static bool cluster_layout(int segs, int* ctas, int* warps) {
+  if (segs <= 1 || segs > kMaxClusterCtas * kMaxClusterWarps) return false;
+  int w = segs < kWarpsPerBlock ? segs : kWarpsPerBlock;
+  int c = (segs + w - 1) / w;
+  if (c > kMaxClusterCtas) {
+    c = kMaxClusterCtas;
+    w = (segs + c - 1) / c;
+  }
+  *ctas = c;
+  *warps = w;
+  return true;
+}
+
+static bool cluster_enabled() {
+  const char* v = getenv("ONYX_B200_CLUSTER");
+  return !(v && v[0] == '0');
+}
+
+template <int DT, bool FAST, int MODE>
+static cudaError_t launch_cluster_t(const ScanParams& p, int warps, cudaStream_t stream, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.rows * p.ctas_per_row), 1, 1);
+  cfg.blockDim = dim3((unsigned)(32 * warps), 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)p.ctas_per_row;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(
+      &cfg, masked_select_cluster_kernel<DT, FAST, MODE, kMaxClusterWarps, kUnroll>, p);
+}
+
+// Launches the cluster kernel when the row fits one cluster; returns false otherwise.
+template <int MODE>
+static bool dispatch_cluster(int dt, bool fast, ScanParams& p, cudaStream_t s, bool pdl,
+                             cudaError_t* err) {
+  if constexpr (MODE == kModeVerify) {
+    return false;
+  } else {
+    int ctas = 0, warps = 0;
+    if (!cluster_enabled() || p.per_group != 1 || !cluster_layout(p.segs, &ctas, &warps))
+      return false;
+    if (dt == kF64 && MODE == kModeKey) return false;
+    p.ctas_per_row = ctas;
+    switch (dt) {
+      case kBF16:
+        *err = fast ? launch_cluster_t<kBF16, true, MODE>(p, warps, s, pdl)
+                    : launch_cluster_t<kBF16, false, MODE>(p, warps, s, pdl);
+        return true;
+      case kF16:
+        *err = fast ? launch_cluster_t<kF16, true, MODE>(p, warps, s, pdl)
+                    : launch_cluster_t<kF16, false, MODE>(p, warps, s, pdl);
+        return true;
+      case kF32:
+        *err = fast ? launch_cluster_t<kF32, true, MODE>(p, warps, s, pdl)
+                    : launch_cluster_t<kF32, false, MODE>(p, warps, s, pdl);
+        return true;
+      case kF64:
+        if constexpr (MODE != kModeKey) {
+          *err = launch_cluster_t<kF64, false, MODE>(p, warps, s, pdl);
+          return true;
+        }
+        return false;
+    }
+    return false;
+  }
+}
+
 template <int MODE>
 static cudaError_t dispatch(int dt, bool fast, const ScanParams& p, cudaStream_t s, bool pdl) {
   switch (dt) {
@@ -924,6 +1071,10 @@ int onyx_masked_argmax(const void* logits, int dtype, int64_t rows, int64_t voca
   p.seg_elems = pl.seg_elems;
   p.out_idx = out_idx;
   p.out_status = out_status;
+  cudaError_t cluster_err = cudaSuccess;
+  if (dispatch_cluster<kModeArgmax>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled(),
+                                    &cluster_err))
+    return finish_launch(cluster_err);  // one cluster per row: no workspace involved
   rc = bind_workspace(p, workspace, workspace_bytes, workspace_bytes_for(rows, rows, pl, 1), rows);
   if (rc) return rc;
   return finish_launch(dispatch<kModeArgmax>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled()));
@@ -958,6 +1109,10 @@ int onyx_gather_masked_argmax(const void* logits, int dtype, int64_t rows, int64
   p.seg_elems = pl.seg_elems;
   p.out_idx = out_idx;
   p.out_status = out_status;
+  cudaError_t cluster_err = cudaSuccess;
+  if (dispatch_cluster<kModeArgmax>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled(),
+                                    &cluster_err))
+    return finish_launch(cluster_err);  // one cluster per row: no workspace involved
   rc = bind_workspace(p, workspace, workspace_bytes, workspace_bytes_for(rows, rows, pl, 1), rows);
   if (rc) return rc;
   return finish_launch(dispatch<kModeArgmax>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled()));
@@ -1043,6 +1198,10 @@ int onyx_vocab_partial_argmax(const void* logits, int dtype, int64_t rows, int64
   p.ctas_per_row = pl.ctas_per_row;
   p.seg_elems = pl.seg_elems;
   p.out_key = reinterpret_cast<unsigned long long*>(out_keys);
+  cudaError_t cluster_err = cudaSuccess;
+  if (dispatch_cluster<kModeKey>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled(),
+                                    &cluster_err))
+    return finish_launch(cluster_err);  // one cluster per row: no workspace involved
   rc = bind_workspace(p, workspace, workspace_bytes, workspace_bytes_for(rows, rows, pl, 1), rows);
   if (rc) return rc;
   return finish_launch(dispatch<kModeKey>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled()));

@@ -217,3 +217,28 @@ def test_workspace_is_left_zeroed_across_layouts(cuda_lib):
         torch.cuda.synchronize()
         for buf in ms._WORKSPACES._buffers.values():
             assert int(torch.count_nonzero(buf)) == 0
+
+
+@pytest.mark.parametrize("path", ["cluster", "ticket"])
+def test_both_cross_cta_combines_match_oracle(path, monkeypatch, cuda_lib):
+    """Rows that fit one thread-block cluster merge CTA partials through distributed shared
+    memory; ONYX_B200_CLUSTER=0 forces the global-ticket merge. Both must agree with the
+    oracle for argmax, gather and shard keys."""
+    monkeypatch.setenv("ONYX_B200_CLUSTER", "1" if path == "cluster" else "0")
+    w = workloads.batched(rows=16)
+    x, m = to_device(w["logits_bf16"], "bf16"), masks_to_device(w["masks"])
+    idx_ref, st_ref = oracle.masked_argmax(w["logits_bf16"], w["masks"], dtype="bf16")
+    r = ms.masked_argmax(x, m)
+    _check(r.token_ids, r.status, idx_ref, st_ref)
+    ids = np.array([3, 0, 15, 7] * 4, np.int32)
+    idx_g, st_g = oracle.gather_masked_argmax(w["logits_bf16"], w["masks"], ids, dtype="bf16")
+    g = ms.gather_masked_argmax(x, m, torch.from_numpy(ids).cuda())
+    _check(g.token_ids, g.status, idx_g, st_g)
+    keys = ms.vocab_partial_keys(x, m, 0)
+    c = ms.combine_partial_keys(keys[None])
+    _check(c.token_ids, c.status, idx_ref, st_ref)
+    # 256,000-token rows need 125 warp segments: 8 CTAs of 16 warps in one cluster
+    w2 = workloads.scaling(rows=4)
+    idx2, st2 = oracle.masked_argmax(w2["logits_bf16"], w2["masks"], dtype="bf16")
+    r2 = ms.masked_argmax(to_device(w2["logits_bf16"], "bf16"), masks_to_device(w2["masks"]))
+    _check(r2.token_ids, r2.status, idx2, st2)
