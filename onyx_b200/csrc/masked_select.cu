@@ -154,113 +154,121 @@ struct Vec16<kF32> {
   __device__ static float scalar(uint32_t raw) { return __uint_as_float(raw); }
 };
 
-// Masked maximum and its lowest index over elements [e0, e1) of one row, by one warp.
+// One warp's segment [e0, e1) of a row, held in registers: 32 lanes x UNROLL 16-byte
+// vectors, every load issued before any is consumed, plus one ragged-tail element per lane
+// when the row length is not a multiple of the vector width.
+//   phase 1 (max_code): masked, NaN-propagating maximum with packed max instructions and no
+//            index bookkeeping; each vector's own maximum is kept.
+//   phase 2 (first_index): given a value code M, the lowest index holding it -- the first
+//            (vector k, lane) whose kept maximum equals M, then the first valid element of
+//            that vector equal to M. Element order within the segment is (k, lane, j).
 template <int DT, int UNROLL>
-__device__ __forceinline__ Partial scan_warp_fast(const void* row_base, const uint32_t* mrow,
-                                                  int64_t e0, int64_t e1, int lane) {
+struct WarpSegment {
   using V = Vec16<DT>;
-  constexpr int E = V::kElems;
-  constexpr int kBytesPerElem = (DT == kF32) ? 4 : 2;
-  constexpr uint32_t kLaneBits = (E == 8) ? 0xFFu : 0xFu;
-  const int64_t nv = (e1 - e0) / E;  // full vectors in this segment
-  const int tail = (int)((e1 - e0) - nv * E);
-  const char* rowc = static_cast<const char*>(row_base);
+  static constexpr int E = V::kElems;
+  static constexpr int kBytesPerElem = (DT == kF32) ? 4 : 2;
+  static constexpr uint32_t kLaneBits = (E == 8) ? 0xFFu : 0xFu;
 
   uint4 x[UNROLL];
-  uint32_t w[UNROLL];
-#pragma unroll
-  for (int k = 0; k < UNROLL; ++k) {
-    const int64_t v = (int64_t)k * 32 + lane;
-    const int64_t e = e0 + v * E;
-    if (v < nv) {
-      x[k] = __ldcs(reinterpret_cast<const uint4*>(rowc + e * kBytesPerElem));
-      w[k] = mrow ? __ldg(mrow + (e >> 5)) : 0xFFFFFFFFu;
-    } else {
-      x[k] = make_uint4(0u, 0u, 0u, 0u);
-      w[k] = 0u;
-    }
-  }
-  // ragged end of the row (vocab not a multiple of the vector width): one scalar
-  // element per lane, at the highest indices of the segment
-  uint32_t tail_raw = 0u, tail_bit = 0u;
-  const int64_t tail_e = e0 + nv * E + lane;
-  if (lane < tail) {
-    if (DT == kF32) {
-      tail_raw = __float_as_uint(__ldg(reinterpret_cast<const float*>(rowc) + tail_e));
-    } else {
-      tail_raw = __ldg(reinterpret_cast<const unsigned short*>(rowc) + tail_e);
-    }
-    tail_bit = mrow ? ((__ldg(mrow + (tail_e >> 5)) >> (tail_e & 31)) & 1u) : 1u;
-  }
-
-  // phase 1: masked maximum, no indices; each vector's own maximum is kept for phase 2
   uint32_t bits[UNROLL];
-  uint32_t any = tail_bit;
-  // segment starts and vector strides are multiples of 32 elements, so a lane's bits
-  // always sit at the same offset in their mask word
-  const uint32_t lane_shift = (uint32_t)(lane * E) & 31u;
-#pragma unroll
-  for (int k = 0; k < UNROLL; ++k) {
-    bits[k] = (w[k] >> lane_shift) & kLaneBits;
-    any |= bits[k];
-  }
-  float tmax;
   uint32_t vmax[UNROLL];  // per-vector masked maximum (packed pair, or f32 bits)
-  if constexpr (DT == kF32) {
-    tmax = __int_as_float(0xFF800000);
+  uint32_t tail_raw, tail_bit;
+  uint32_t tord;  // this lane's maximum as an order code, 0 = no valid token
+  int64_t e0, nv;
+  int lane;
+
+  __device__ __forceinline__ void load(const void* row_base, const uint32_t* mrow, int64_t e0_,
+                                       int64_t e1, int lane_) {
+    e0 = e0_;
+    lane = lane_;
+    nv = (e1 - e0) / E;  // full vectors in this segment
+    const int tail = (int)((e1 - e0) - nv * E);
+    const char* rowc = static_cast<const char*>(row_base);
+    uint32_t w[UNROLL];
 #pragma unroll
     for (int k = 0; k < UNROLL; ++k) {
-      const float vm = V::masked_max(x[k], bits[k]);
-      vmax[k] = __float_as_uint(vm);
-      tmax = max_nan_f32(tmax, vm);
+      const int64_t v = (int64_t)k * 32 + lane;
+      const int64_t e = e0 + v * E;
+      if (v < nv) {
+        x[k] = __ldcs(reinterpret_cast<const uint4*>(rowc + e * kBytesPerElem));
+        w[k] = mrow ? __ldg(mrow + (e >> 5)) : 0xFFFFFFFFu;
+      } else {
+        x[k] = make_uint4(0u, 0u, 0u, 0u);
+        w[k] = 0u;
+      }
     }
-  } else {
-    uint32_t pm = V::kNegInfPair;
-#pragma unroll
-    for (int k = 0; k < UNROLL; ++k) {
-      vmax[k] = V::masked_pair_max(x[k], bits[k]);
-      pm = V::pmax(pm, vmax[k]);
+    tail_raw = 0u;
+    tail_bit = 0u;
+    if (lane < tail) {
+      const int64_t te = e0 + nv * E + lane;
+      if (DT == kF32) {
+        tail_raw = __float_as_uint(__ldg(reinterpret_cast<const float*>(rowc) + te));
+      } else {
+        tail_raw = __ldg(reinterpret_cast<const unsigned short*>(rowc) + te);
+      }
+      tail_bit = mrow ? ((__ldg(mrow + (te >> 5)) >> (te & 31)) & 1u) : 1u;
     }
-    tmax = V::pair_to_f32_max(pm);
-  }
-  if (tail_bit) tmax = max_nan_f32(tmax, V::scalar(tail_raw));
-  // order code 0 = this lane holds no valid token
-  const uint32_t tord = any ? ord32(tmax) : 0u;
-  const uint32_t M = __reduce_max_sync(kFull, tord);
-
-  Partial part;
-  part.flags = M ? kFlagAny : 0u;
-  part.ord = M;
-  part.idx = 0xFFFFFFFFu;
-  if (M == 0u || M == kOrd32NaN) return part;
-
-  // phase 2, warp-wide: the lowest (vector k, lane) whose kept vector maximum equals M
-  // (a vector with valid elements reaches M only through a valid element equal to M),
-  // then the lowest valid element of that vector equal to M. Element order within the
-  // segment is (k, lane, j), so this is the lowest index. Equality is float equality:
-  // -0.0 and +0.0 match alike.
-  const float mf = __uint_as_float((M & 0x80000000u) ? (M & 0x7FFFFFFFu) : ~M);
-  uint32_t key = 0xFFFFFFFFu;
-  uint32_t m2 = 0u;
-  if constexpr (DT == kF32) {
+    // segment starts and vector strides are multiples of 32 elements, so a lane's bits
+    // always sit at the same offset in their mask word
+    const uint32_t lane_shift = (uint32_t)(lane * E) & 31u;
 #pragma unroll
-    for (int k = UNROLL - 1; k >= 0; --k)
-      if (bits[k] && __uint_as_float(vmax[k]) == mf) key = ((uint32_t)k << 5) | lane;
-  } else {
-    const uint32_t h = V::from_f32(mf);
-    m2 = h | (h << 16);
-#pragma unroll
-    for (int k = UNROLL - 1; k >= 0; --k)
-      if (bits[k] && V::eq_mask(vmax[k], m2)) key = ((uint32_t)k << 5) | lane;
+    for (int k = 0; k < UNROLL; ++k) bits[k] = (w[k] >> lane_shift) & kLaneBits;
   }
-  if (key == 0xFFFFFFFFu && tail_bit && ord32(V::scalar(tail_raw)) == M)
-    key = ((uint32_t)UNROLL << 5) | lane;  // the ragged tail follows every full vector
-  const uint32_t win = __reduce_min_sync(kFull, key);
-  const int wk = (int)(win >> 5), wl = (int)(win & 31u);
-  uint32_t cand;
-  if (wk >= UNROLL) {
-    cand = (uint32_t)(e0 + nv * E + wl);
-  } else {
+
+  // warp maximum as an order code (0: no valid token in the segment)
+  __device__ __forceinline__ uint32_t max_code() {
+    uint32_t any = tail_bit;
+#pragma unroll
+    for (int k = 0; k < UNROLL; ++k) any |= bits[k];
+    float tmax;
+    if constexpr (DT == kF32) {
+      tmax = __int_as_float(0xFF800000);
+#pragma unroll
+      for (int k = 0; k < UNROLL; ++k) {
+        const float vm = V::masked_max(x[k], bits[k]);
+        vmax[k] = __float_as_uint(vm);
+        tmax = max_nan_f32(tmax, vm);
+      }
+    } else {
+      uint32_t pm = V::kNegInfPair;
+#pragma unroll
+      for (int k = 0; k < UNROLL; ++k) {
+        vmax[k] = V::masked_pair_max(x[k], bits[k]);
+        pm = V::pmax(pm, vmax[k]);
+      }
+      tmax = V::pair_to_f32_max(pm);
+    }
+    if (tail_bit) tmax = max_nan_f32(tmax, V::scalar(tail_raw));
+    tord = any ? ord32(tmax) : 0u;
+    return __reduce_max_sync(kFull, tord);
+  }
+
+  // lowest index of the segment whose valid value has order code M (a code of a real,
+  // non-NaN value); 0xFFFFFFFF if the segment holds none. Warp-wide, lanes converged.
+  // Equality is float equality, so -0.0 and +0.0 match alike.
+  __device__ __forceinline__ uint32_t first_index(uint32_t M) {
+    const float mf = __uint_as_float((M & 0x80000000u) ? (M & 0x7FFFFFFFu) : ~M);
+    uint32_t key = 0xFFFFFFFFu;
+    uint32_t m2 = 0u;
+    if (tord == M) {  // only lanes whose maximum is M can hold it
+      if constexpr (DT == kF32) {
+#pragma unroll
+        for (int k = UNROLL - 1; k >= 0; --k)
+          if (bits[k] && __uint_as_float(vmax[k]) == mf) key = ((uint32_t)k << 5) | lane;
+      } else {
+        const uint32_t h = V::from_f32(mf);
+        m2 = h | (h << 16);
+#pragma unroll
+        for (int k = UNROLL - 1; k >= 0; --k)
+          if (bits[k] && V::eq_mask(vmax[k], m2)) key = ((uint32_t)k << 5) | lane;
+      }
+      if (key == 0xFFFFFFFFu && tail_bit && ord32(V::scalar(tail_raw)) == M)
+        key = ((uint32_t)UNROLL << 5) | lane;  // the ragged tail follows every full vector
+    }
+    const uint32_t win = __reduce_min_sync(kFull, key);
+    if (win == 0xFFFFFFFFu) return 0xFFFFFFFFu;
+    const int wk = (int)(win >> 5), wl = (int)(win & 31u);
+    if (wk >= UNROLL) return (uint32_t)(e0 + nv * E + wl);
     uint4 xv = x[0];
     uint32_t bv = bits[0];
 #pragma unroll
@@ -276,6 +284,8 @@ __device__ __forceinline__ Partial scan_warp_fast(const void* row_base, const ui
       if ((bv & 2u) && __uint_as_float(xv.y) == mf) j = 1;
       if ((bv & 1u) && __uint_as_float(xv.x) == mf) j = 0;
     } else {
+      const uint32_t h = V::from_f32(mf);
+      m2 = h | (h << 16);
       uint32_t m01, m23, m45, m67;
       expand4_16(bv, m01, m23);
       expand4_16(bv >> 4, m45, m67);
@@ -289,9 +299,21 @@ __device__ __forceinline__ Partial scan_warp_fast(const void* row_base, const ui
       j = q ? (__ffsll((long long)q) - 1) >> 4 : 4 + ((__ffsll((long long)r) - 1) >> 4);
     }
     j = __shfl_sync(kFull, j, wl);
-    cand = (uint32_t)(e0 + ((int64_t)wk * 32 + wl) * E + j);
+    return (uint32_t)(e0 + ((int64_t)wk * 32 + wl) * E + j);
   }
-  part.idx = cand;
+};
+
+// Masked maximum and its lowest index over elements [e0, e1) of one row, by one warp.
+template <int DT, int UNROLL>
+__device__ __forceinline__ Partial scan_warp_fast(const void* row_base, const uint32_t* mrow,
+                                                  int64_t e0, int64_t e1, int lane) {
+  WarpSegment<DT, UNROLL> seg;
+  seg.load(row_base, mrow, e0, e1, lane);
+  const uint32_t M = seg.max_code();
+  Partial part;
+  part.flags = M ? kFlagAny : 0u;
+  part.ord = M;
+  part.idx = (M == 0u || M == kOrd32NaN) ? 0xFFFFFFFFu : seg.first_index(M);
   return part;
 }
 
@@ -330,35 +352,65 @@ __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v)
   return v;
 }
 
+// One warp's segment [e0, e1) on the generic path: coalesced scalar loads, any alignment,
+// any dtype; first_index re-reads the segment (it is still in L1/L2).
+template <int DT>
+struct GenericSegment {
+  const void* row;
+  const uint32_t* mrow;
+  int64_t e0, e1;
+  int lane;
+  unsigned long long tbest;  // lane maximum as an order code, 0 = no valid token
+
+  __device__ __forceinline__ void load(const void* row_base, const uint32_t* mrow_, int64_t e0_,
+                                       int64_t e1_, int lane_) {
+    row = row_base;
+    mrow = mrow_;
+    e0 = e0_;
+    e1 = e1_;
+    lane = lane_;
+  }
+
+  __device__ __forceinline__ uint32_t bit(int64_t e) const {
+    return mrow ? ((__ldg(mrow + (e >> 5)) >> (e & 31)) & 1u) : 1u;
+  }
+
+  __device__ __forceinline__ unsigned long long max_code() {
+    tbest = 0ull;
+    for (int64_t e = e0 + lane; e < e1; e += 32) {
+      if (bit(e)) {
+        const unsigned long long o = elem_ord<DT>(load_elem<DT>(row, e));
+        tbest = o > tbest ? o : tbest;
+      }
+    }
+    return warp_max_u64(tbest);
+  }
+
+  __device__ __forceinline__ uint32_t first_index(unsigned long long M) {
+    uint32_t cand = 0xFFFFFFFFu;
+    if (tbest == M) {
+      for (int64_t e = e0 + lane; e < e1; e += 32) {
+        if (bit(e) && elem_ord<DT>(load_elem<DT>(row, e)) == M) {
+          cand = (uint32_t)e;
+          break;
+        }
+      }
+    }
+    return __reduce_min_sync(kFull, cand);
+  }
+};
+
 template <int DT>
 __device__ __forceinline__ Partial scan_warp_generic(const void* row_base, const uint32_t* mrow,
                                                      int64_t e0, int64_t e1, int lane) {
-  unsigned long long tbest = 0ull;  // 0 = no valid token seen by this lane
-  for (int64_t e = e0 + lane; e < e1; e += 32) {
-    const uint32_t bit = mrow ? ((__ldg(mrow + (e >> 5)) >> (e & 31)) & 1u) : 1u;
-    if (bit) {
-      const unsigned long long o = elem_ord<DT>(load_elem<DT>(row_base, e));
-      tbest = o > tbest ? o : tbest;
-    }
-  }
-  const unsigned long long M = warp_max_u64(tbest);
+  GenericSegment<DT> seg;
+  seg.load(row_base, mrow, e0, e1, lane);
+  const unsigned long long M = seg.max_code();
   const unsigned long long nan_code = (DT == kF64) ? kOrd64NaN : (unsigned long long)kOrd32NaN;
   Partial part;
   part.flags = M ? kFlagAny : 0u;
   part.ord = M;
-  part.idx = 0xFFFFFFFFu;
-  if (M == 0ull || M == nan_code) return part;
-  uint32_t cand = 0xFFFFFFFFu;
-  if (tbest == M) {
-    for (int64_t e = e0 + lane; e < e1; e += 32) {
-      const uint32_t bit = mrow ? ((__ldg(mrow + (e >> 5)) >> (e & 31)) & 1u) : 1u;
-      if (bit && elem_ord<DT>(load_elem<DT>(row_base, e)) == M) {
-        cand = (uint32_t)e;
-        break;
-      }
-    }
-  }
-  part.idx = __reduce_min_sync(kFull, cand);
+  part.idx = (M == 0ull || M == nan_code) ? 0xFFFFFFFFu : seg.first_index(M);
   return part;
 }
 
@@ -573,27 +625,43 @@ __global__ void __launch_bounds__(MAXWARPS * 32)
     finalize_group<MODE, DT == kF64>(p, group, nullptr, lane);
 }
 
-// Same selection with the CTAs of one row grouped in a thread-block cluster: each CTA
-// stores its partial straight into rank 0's shared memory (distributed shared memory) and
-// one hardware cluster barrier replaces the global ticket -- no atomics, no fences, no
-// workspace. Used for the argmax / gather / shard-key modes when a row needs at most
-// kMaxClusterCtas CTAs.
+// Same selection with the CTAs of one row grouped in a thread-block cluster, which lets
+// the index search wait for the row maximum:
+//   1. every warp computes its segment maximum (phase 1 only);
+//   2. each CTA's maximum is written into every CTA of the cluster through distributed
+//      shared memory; after one cluster barrier every warp knows the row maximum;
+//   3. only warps whose own maximum equals it (normally one per row) search their
+//      registers for its lowest index;
+//   4. each CTA's lowest index goes to rank 0's shared memory; after a second barrier
+//      rank 0 writes the outputs.
+// No atomics, no fences, no workspace. Used for the argmax / gather / shard-key modes when
+// a row needs at most kMaxClusterCtas CTAs.
 constexpr int kMaxClusterCtas = 8;
 
-template <int DT, bool FAST, int MODE, int MAXWARPS, int UNROLL>
-__global__ void __launch_bounds__(MAXWARPS * 32)
-    masked_select_cluster_kernel(const ScanParams p) {
-  static_assert(MODE != kModeVerify, "verify groups span several rows");
+__device__ __forceinline__ unsigned long long warp_min_u64(unsigned long long v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(kFull, v, o);
+    v = other < v ? other : v;
+  }
+  return v;
+}
+
+template <int DT, int MODE, int MAXWARPS, class Seg>
+__device__ __forceinline__ void cluster_select(const ScanParams& p) {
   namespace cg = cooperative_groups;
-  __shared__ Partial s_part[MAXWARPS];
-  __shared__ Partial s_cta[kMaxClusterCtas];
+  __shared__ unsigned long long s_wmax[MAXWARPS];
+  __shared__ unsigned long long s_cmax[kMaxClusterCtas];  // every CTA's maximum, in every CTA
+  __shared__ uint32_t s_widx[MAXWARPS];
+  __shared__ uint32_t s_cidx[kMaxClusterCtas];  // rank 0: every CTA's lowest index
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
+  const int C = p.ctas_per_row;  // cluster size
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int nwarps = blockDim.x >> 5;
-  const int64_t row = blockIdx.x / p.ctas_per_row;  // one cluster per row
-  const int seg = rank * nwarps + warp;
+  const int64_t row = blockIdx.x / C;  // one cluster per row
+  const int seg_id = rank * nwarps + warp;
 
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
@@ -611,32 +679,58 @@ __global__ void __launch_bounds__(MAXWARPS * 32)
     }
   }
 
-  Partial part = empty_partial();
-  if (bad_state) {
-    part.flags = kFlagBadState;
-  } else if (seg < p.segs) {  // warp-uniform
-    const int64_t e0 = (int64_t)seg * p.seg_elems;
-    const int64_t e1 = min(e0 + p.seg_elems, p.vocab);
-    if constexpr (FAST) {
-      part = scan_warp_fast<DT, UNROLL>(row_base, mrow, e0, e1, lane);
-    } else {
-      part = scan_warp_generic<DT>(row_base, mrow, e0, e1, lane);
-    }
-    if (part.idx != 0xFFFFFFFFu) part.idx += (uint32_t)p.idx_offset;
+  // 1. segment maximum
+  Seg seg;
+  const bool active = !bad_state && seg_id < p.segs;  // warp-uniform
+  unsigned long long wmax = 0ull;
+  if (active) {
+    const int64_t e0 = (int64_t)seg_id * p.seg_elems;
+    seg.load(row_base, mrow, e0, min(e0 + p.seg_elems, p.vocab), lane);
+    wmax = (unsigned long long)seg.max_code();
   }
-
   asm volatile("griddepcontrol.launch_dependents;" :::);
 
-  if (lane == 0) s_part[warp] = part;
+  // 2. row maximum through every CTA's shared memory
+  if (lane == 0) s_wmax[warp] = wmax;
   __syncthreads();
   if (warp == 0) {
-    part = warp_merge(lane < nwarps ? s_part[lane] : empty_partial());
-    if (lane == 0) *cluster.map_shared_rank(&s_cta[rank], 0) = part;
+    const unsigned long long cmax = warp_max_u64(lane < nwarps ? s_wmax[lane] : 0ull);
+    if (lane < C) *cluster.map_shared_rank(&s_cmax[rank], lane) = cmax;
   }
-  cluster.sync();  // every CTA's partial has landed in rank 0's shared memory
+  cluster.sync();
+  const unsigned long long M = warp_max_u64(lane < C ? s_cmax[lane] : 0ull);
+  const unsigned long long nan_code = (DT == kF64) ? kOrd64NaN : (unsigned long long)kOrd32NaN;
+
+  // 3. lowest index of the maximum, by the warps that hold it
+  uint32_t widx = 0xFFFFFFFFu;
+  if (active && wmax == M && M != 0ull && M != nan_code) widx = seg.first_index(M);
+  if (lane == 0) s_widx[warp] = widx;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t cidx = __reduce_min_sync(kFull, lane < nwarps ? s_widx[lane] : 0xFFFFFFFFu);
+    if (lane == 0) *cluster.map_shared_rank(&s_cidx[rank], 0) = cidx;
+  }
+  cluster.sync();
+
+  // 4. outputs
   if (rank == 0 && warp == 0) {
-    part = warp_merge(lane < p.ctas_per_row ? s_cta[lane] : empty_partial());
+    Partial part;
+    part.flags = (bad_state ? kFlagBadState : 0u) | (M ? kFlagAny : 0u);
+    part.ord = M;
+    const uint32_t idx = (uint32_t)warp_min_u64(lane < C ? s_cidx[lane] : 0xFFFFFFFFull);
+    part.idx = idx == 0xFFFFFFFFu ? idx : idx + (uint32_t)p.idx_offset;
     finalize_group<MODE, DT == kF64>(p, row, &part, lane);
+  }
+}
+
+template <int DT, bool FAST, int MODE, int MAXWARPS, int UNROLL>
+__global__ void __launch_bounds__(MAXWARPS * 32, 1024 / (MAXWARPS * 32))
+    masked_select_cluster_kernel(const ScanParams p) {
+  static_assert(MODE != kModeVerify, "verify groups span several rows");
+  if constexpr (FAST) {
+    cluster_select<DT, MODE, MAXWARPS, WarpSegment<DT, UNROLL>>(p);
+  } else {
+    cluster_select<DT, MODE, MAXWARPS, GenericSegment<DT>>(p);
   }
 }
 
