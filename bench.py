@@ -38,8 +38,8 @@ METRIC = "masked-argmax rows/s and HBM GB/s (vs ~8 TB/s), B=64 V=128256 bf16"
 UNIT = "rows/s"
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from an ncu capture of the
-# dominant kernel (profiles/masked_select_batched_bf16.md); None until captured.
-NCU_TRAFFIC_PER_LAUNCH: dict[str, float | None] = {"batched": None}
+# dominant kernel (profiles/masked_select_batched_bf16.md).
+NCU_TRAFFIC_PER_LAUNCH: dict[str, float | None] = {"batched": 17460992.0}
 
 FALLBACK_HBM_GBS = 6650.0
 
@@ -88,7 +88,7 @@ def _peaks() -> tuple[float, str]:
 class ClockSampler:
     """Samples SM clock and throttle reasons through NVML while the timed region runs."""
 
-    def __init__(self, device_index: int, period_s: float = 0.002) -> None:
+    def __init__(self, device_index: int, period_s: float = 0.0005) -> None:
         self.samples: list[tuple[int, int]] = []
         self.period = period_s
         self._stop = threading.Event()
