@@ -171,7 +171,6 @@ struct WarpSegment {
 
   uint4 x[UNROLL];
   uint32_t bits[UNROLL];
-  uint32_t vmax[UNROLL];  // per-vector masked maximum (packed pair, or f32 bits)
   uint32_t tail_raw, tail_bit;
   uint32_t tord;  // this lane's maximum as an order code, 0 = no valid token
   int64_t e0, nv;
@@ -224,18 +223,11 @@ struct WarpSegment {
     if constexpr (DT == kF32) {
       tmax = __int_as_float(0xFF800000);
 #pragma unroll
-      for (int k = 0; k < UNROLL; ++k) {
-        const float vm = V::masked_max(x[k], bits[k]);
-        vmax[k] = __float_as_uint(vm);
-        tmax = max_nan_f32(tmax, vm);
-      }
+      for (int k = 0; k < UNROLL; ++k) tmax = max_nan_f32(tmax, V::masked_max(x[k], bits[k]));
     } else {
       uint32_t pm = V::kNegInfPair;
 #pragma unroll
-      for (int k = 0; k < UNROLL; ++k) {
-        vmax[k] = V::masked_pair_max(x[k], bits[k]);
-        pm = V::pmax(pm, vmax[k]);
-      }
+      for (int k = 0; k < UNROLL; ++k) pm = V::pmax(pm, V::masked_pair_max(x[k], bits[k]));
       tmax = V::pair_to_f32_max(pm);
     }
     if (tail_bit) tmax = max_nan_f32(tmax, V::scalar(tail_raw));
@@ -251,16 +243,19 @@ struct WarpSegment {
     uint32_t key = 0xFFFFFFFFu;
     uint32_t m2 = 0u;
     if (tord == M) {  // only lanes whose maximum is M can hold it
+      // each vector's masked maximum is recomputed here rather than kept from phase 1:
+      // only the lanes holding the maximum get this far
       if constexpr (DT == kF32) {
 #pragma unroll
         for (int k = UNROLL - 1; k >= 0; --k)
-          if (bits[k] && __uint_as_float(vmax[k]) == mf) key = ((uint32_t)k << 5) | lane;
+          if (bits[k] && V::masked_max(x[k], bits[k]) == mf) key = ((uint32_t)k << 5) | lane;
       } else {
         const uint32_t h = V::from_f32(mf);
         m2 = h | (h << 16);
 #pragma unroll
         for (int k = UNROLL - 1; k >= 0; --k)
-          if (bits[k] && V::eq_mask(vmax[k], m2)) key = ((uint32_t)k << 5) | lane;
+          if (bits[k] && V::eq_mask(V::masked_pair_max(x[k], bits[k]), m2))
+            key = ((uint32_t)k << 5) | lane;
       }
       if (key == 0xFFFFFFFFu && tail_bit && ord32(V::scalar(tail_raw)) == M)
         key = ((uint32_t)UNROLL << 5) | lane;  // the ragged tail follows every full vector
@@ -480,11 +475,11 @@ __device__ __forceinline__ Partial reduce_member(Partial* base, int segs, int la
 // has a single segment (no workspace).
 template <int MODE, bool IS64>
 __device__ void finalize_group(const ScanParams& p, int64_t group, const Partial* single,
-                               int lane) {
+                               int lane, int parts) {
   const int P = p.per_group;
-  Partial* base = single ? nullptr : p.ws_part + group * (int64_t)P * p.ctas_per_row;
+  Partial* base = single ? nullptr : p.ws_part + group * (int64_t)P * parts;
   if constexpr (MODE == kModeArgmax || MODE == kModeKey) {
-    const Partial r = single ? *single : reduce_member(base, p.ctas_per_row, lane);
+    const Partial r = single ? *single : reduce_member(base, parts, lane);
     if (lane != 0) return;
     if constexpr (MODE == kModeArgmax) {
       decode_partial(r, IS64, &p.out_idx[group], &p.out_status[group]);
@@ -502,8 +497,7 @@ __device__ void finalize_group(const ScanParams& p, int64_t group, const Partial
     uint32_t st = 0u;
     bool decided = false;
     for (int i = 0; i < P; ++i) {
-      const Partial r =
-          single ? *single : reduce_member(base + (int64_t)i * p.ctas_per_row, p.ctas_per_row, lane);
+      const Partial r = single ? *single : reduce_member(base + (int64_t)i * parts, parts, lane);
       if (decided) continue;
       int32_t sel;
       uint32_t rs;
@@ -618,24 +612,24 @@ __global__ void __launch_bounds__(MAXWARPS * 32)
 
   const uint32_t total = (uint32_t)(p.per_group * p.ctas_per_row);
   if (total == 1u) {
-    finalize_group<MODE, DT == kF64>(p, group, &part, lane);
+    finalize_group<MODE, DT == kF64>(p, group, &part, lane, p.ctas_per_row);
     return;
   }
   if (take_ticket(p.ws_part + blockIdx.x, part, p.ws_count + group, total, lane))
-    finalize_group<MODE, DT == kF64>(p, group, nullptr, lane);
+    finalize_group<MODE, DT == kF64>(p, group, nullptr, lane, p.ctas_per_row);
 }
 
-// Same selection with the CTAs of one row grouped in a thread-block cluster, which lets
-// the index search wait for the row maximum:
-//   1. every warp computes its segment maximum (phase 1 only);
+// Cluster kernel: the CTAs of one thread-block cluster split one row between them (one
+// warp per segment), which lets the index search wait for the row maximum:
+//   1. every warp loads its segment and computes the segment maximum (phase 1 only);
 //   2. each CTA's maximum is written into every CTA of the cluster through distributed
-//      shared memory; after one cluster barrier every warp knows the row maximum;
+//      shared memory; after a cluster barrier every warp knows the row maximum;
 //   3. only warps whose own maximum equals it (normally one per row) search their
 //      registers for its lowest index;
 //   4. each CTA's lowest index goes to rank 0's shared memory; after a second barrier
-//      rank 0 writes the outputs.
+//      rank 0 writes the row's outputs.
 // No atomics, no fences, no workspace. Used for the argmax / gather / shard-key modes when
-// a row needs at most kMaxClusterCtas CTAs.
+// a row needs at most kMaxClusterCtas x kMaxClusterWarps warp segments.
 constexpr int kMaxClusterCtas = 8;
 
 __device__ __forceinline__ unsigned long long warp_min_u64(unsigned long long v) {
@@ -645,6 +639,27 @@ __device__ __forceinline__ unsigned long long warp_min_u64(unsigned long long v)
     v = other < v ? other : v;
   }
   return v;
+}
+
+// Where row `row` (group-major) and its mask live; bad_state for out-of-range DFA states.
+template <int DT>
+__device__ __forceinline__ void locate_row(const ScanParams& p, int64_t row, const void** base,
+                                           const uint32_t** mrow, bool* bad_state) {
+  using St = typename Elem<DT>::storage;
+  const int64_t group = row / p.per_group;
+  const int64_t member = row - group * p.per_group;
+  *base = static_cast<const St*>(p.logits) + group * p.group_stride + member * p.row_stride;
+  *mrow = nullptr;
+  *bad_state = false;
+  if (p.mask) {
+    if (p.state_ids) {
+      const int32_t s = __ldg(p.state_ids + row);
+      *bad_state = (s < 0) || ((int64_t)s >= p.n_states);
+      *mrow = p.mask + (*bad_state ? 0 : (int64_t)s * p.mask_row_stride);
+    } else {
+      *mrow = p.mask + group * p.mask_group_stride + member * p.mask_row_stride;
+    }
+  }
 }
 
 template <int DT, int MODE, int MAXWARPS, class Seg>
@@ -662,22 +677,14 @@ __device__ __forceinline__ void cluster_select(const ScanParams& p) {
   const int nwarps = blockDim.x >> 5;
   const int64_t row = blockIdx.x / C;  // one cluster per row
   const int seg_id = rank * nwarps + warp;
+  const unsigned long long nan_code = (DT == kF64) ? kOrd64NaN : (unsigned long long)kOrd32NaN;
 
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  using St = typename Elem<DT>::storage;
-  const St* row_base = static_cast<const St*>(p.logits) + row * p.group_stride;
-  const uint32_t* mrow = nullptr;
-  bool bad_state = false;
-  if (p.mask) {
-    if (p.state_ids) {
-      const int32_t s = __ldg(p.state_ids + row);
-      bad_state = (s < 0) || ((int64_t)s >= p.n_states);
-      mrow = p.mask + (bad_state ? 0 : (int64_t)s * p.mask_row_stride);
-    } else {
-      mrow = p.mask + row * p.mask_group_stride;
-    }
-  }
+  const void* row_base;
+  const uint32_t* mrow;
+  bool bad_state;
+  locate_row<DT>(p, row, &row_base, &mrow, &bad_state);
 
   // 1. segment maximum
   Seg seg;
@@ -699,7 +706,6 @@ __device__ __forceinline__ void cluster_select(const ScanParams& p) {
   }
   cluster.sync();
   const unsigned long long M = warp_max_u64(lane < C ? s_cmax[lane] : 0ull);
-  const unsigned long long nan_code = (DT == kF64) ? kOrd64NaN : (unsigned long long)kOrd32NaN;
 
   // 3. lowest index of the maximum, by the warps that hold it
   uint32_t widx = 0xFFFFFFFFu;
@@ -719,7 +725,7 @@ __device__ __forceinline__ void cluster_select(const ScanParams& p) {
     part.ord = M;
     const uint32_t idx = (uint32_t)warp_min_u64(lane < C ? s_cidx[lane] : 0xFFFFFFFFull);
     part.idx = idx == 0xFFFFFFFFu ? idx : idx + (uint32_t)p.idx_offset;
-    finalize_group<MODE, DT == kF64>(p, row, &part, lane);
+    finalize_group<MODE, DT == kF64>(p, row, &part, lane, 1);
   }
 }
 
@@ -961,7 +967,7 @@ constexpr int kMaxClusterWarps = 16;
 // Cluster layout for one row: at most kMaxClusterCtas CTAs of at most kMaxClusterWarps warps,
 // one warp per segment. False when the row needs more (the ticket kernel handles it).
 static bool cluster_layout(int segs, int* ctas, int* warps) {
-  if (segs <= 1 || segs > kMaxClusterCtas * kMaxClusterWarps) return false;
+  if (segs < 1 || segs > kMaxClusterCtas * kMaxClusterWarps) return false;
   int w = segs < kWarpsPerBlock ? segs : kWarpsPerBlock;
   int c = (segs + w - 1) / w;
   if (c > kMaxClusterCtas) {
@@ -1253,6 +1259,8 @@ int onyx_spec_verify(const void* logits, int dtype, int64_t batch, int64_t gamma
   p.bonus = bonus ? 1 : 0;
   p.accept_len = accept_len;
   p.correction = correction;
+  // verify grids span several waves; the all-ticket merge measured faster there than one
+  // cluster per row
   const int rc = bind_workspace(p, workspace, workspace_bytes,
                                 workspace_bytes_for(p.rows, batch, pl, P), batch);
   if (rc) return rc;
