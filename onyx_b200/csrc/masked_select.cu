@@ -173,33 +173,44 @@ struct WarpSegment {
   uint32_t bits[UNROLL];
   uint32_t tail_raw, tail_bit;
   uint32_t tord;  // this lane's maximum as an order code, 0 = no valid token
-  int64_t e0, nv;
+  uint32_t e0, nv;  // in-row indices are 32-bit: rows are shorter than 2^31 elements
   int lane;
 
   __device__ __forceinline__ void load(const void* row_base, const uint32_t* mrow, int64_t e0_,
                                        int64_t e1, int lane_) {
-    e0 = e0_;
+    e0 = (uint32_t)e0_;
     lane = lane_;
-    nv = (e1 - e0) / E;  // full vectors in this segment
-    const int tail = (int)((e1 - e0) - nv * E);
+    const uint32_t n = (uint32_t)(e1 - e0_);
+    nv = n / E;  // full vectors in this segment
+    const int tail = (int)(n - nv * E);
     const char* rowc = static_cast<const char*>(row_base);
+    // the lane's first vector and, in each group of 32 vectors, its mask word: segment
+    // starts and vector strides are multiples of 32 elements
+    const uint4* vp = reinterpret_cast<const uint4*>(rowc + (size_t)e0 * kBytesPerElem) + lane;
+    const uint32_t* mp = mrow ? mrow + (e0 >> 5) + ((lane * E) >> 5) : nullptr;
     uint32_t w[UNROLL];
+    if (nv == (uint32_t)(UNROLL * 32)) {  // full segment (warp-uniform): no bounds checks
 #pragma unroll
-    for (int k = 0; k < UNROLL; ++k) {
-      const int64_t v = (int64_t)k * 32 + lane;
-      const int64_t e = e0 + v * E;
-      if (v < nv) {
-        x[k] = __ldcs(reinterpret_cast<const uint4*>(rowc + e * kBytesPerElem));
-        w[k] = mrow ? __ldg(mrow + (e >> 5)) : 0xFFFFFFFFu;
-      } else {
-        x[k] = make_uint4(0u, 0u, 0u, 0u);
-        w[k] = 0u;
+      for (int k = 0; k < UNROLL; ++k) {
+        x[k] = __ldcs(vp + k * 32);
+        w[k] = mp ? __ldg(mp + k * E) : 0xFFFFFFFFu;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < UNROLL; ++k) {
+        if ((uint32_t)(k * 32 + lane) < nv) {
+          x[k] = __ldcs(vp + k * 32);
+          w[k] = mp ? __ldg(mp + k * E) : 0xFFFFFFFFu;
+        } else {
+          x[k] = make_uint4(0u, 0u, 0u, 0u);
+          w[k] = 0u;
+        }
       }
     }
     tail_raw = 0u;
     tail_bit = 0u;
     if (lane < tail) {
-      const int64_t te = e0 + nv * E + lane;
+      const uint32_t te = e0 + nv * E + lane;
       if (DT == kF32) {
         tail_raw = __float_as_uint(__ldg(reinterpret_cast<const float*>(rowc) + te));
       } else {
@@ -207,8 +218,6 @@ struct WarpSegment {
       }
       tail_bit = mrow ? ((__ldg(mrow + (te >> 5)) >> (te & 31)) & 1u) : 1u;
     }
-    // segment starts and vector strides are multiples of 32 elements, so a lane's bits
-    // always sit at the same offset in their mask word
     const uint32_t lane_shift = (uint32_t)(lane * E) & 31u;
 #pragma unroll
     for (int k = 0; k < UNROLL; ++k) bits[k] = (w[k] >> lane_shift) & kLaneBits;
@@ -263,7 +272,7 @@ struct WarpSegment {
     const uint32_t win = __reduce_min_sync(kFull, key);
     if (win == 0xFFFFFFFFu) return 0xFFFFFFFFu;
     const int wk = (int)(win >> 5), wl = (int)(win & 31u);
-    if (wk >= UNROLL) return (uint32_t)(e0 + nv * E + wl);
+    if (wk >= UNROLL) return e0 + nv * E + (uint32_t)wl;
     uint4 xv = x[0];
     uint32_t bv = bits[0];
 #pragma unroll
@@ -294,7 +303,7 @@ struct WarpSegment {
       j = q ? (__ffsll((long long)q) - 1) >> 4 : 4 + ((__ffsll((long long)r) - 1) >> 4);
     }
     j = __shfl_sync(kFull, j, wl);
-    return (uint32_t)(e0 + ((int64_t)wk * 32 + wl) * E + j);
+    return e0 + (uint32_t)((wk * 32 + wl) * E + j);
   }
 };
 
@@ -555,11 +564,12 @@ __global__ void __launch_bounds__(MAXWARPS * 32)
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int nwarps = blockDim.x >> 5;
-  const int64_t row = blockIdx.x / p.ctas_per_row;
-  const int cta = (int)(blockIdx.x - row * p.ctas_per_row);
+  const uint32_t row = blockIdx.x / (uint32_t)p.ctas_per_row;
+  const int cta = (int)(blockIdx.x - row * (uint32_t)p.ctas_per_row);
   const int seg = cta * nwarps + warp;
-  const int64_t group = row / p.per_group;
-  const int64_t member = row - group * p.per_group;
+  // rows per group exceed one only when verifying
+  const uint32_t group = (MODE == kModeVerify) ? row / (uint32_t)p.per_group : row;
+  const uint32_t member = row - group * (uint32_t)p.per_group;
 
   // Programmatic dependent launch: everything this kernel reads may come from the
   // preceding kernel in the stream.
@@ -620,34 +630,27 @@ __global__ void __launch_bounds__(MAXWARPS * 32)
 }
 
 // Cluster kernel: the CTAs of one thread-block cluster split one row between them (one
-// warp per segment), which lets the index search wait for the row maximum:
-//   1. every warp loads its segment and computes the segment maximum (phase 1 only);
-//   2. each CTA's maximum is written into every CTA of the cluster through distributed
-//      shared memory; after a cluster barrier every warp knows the row maximum;
-//   3. only warps whose own maximum equals it (normally one per row) search their
-//      registers for its lowest index;
-//   4. each CTA's lowest index goes to rank 0's shared memory; after a second barrier
-//      rank 0 writes the row's outputs.
+// warp per segment):
+//   1. every warp loads its segment and computes the segment maximum;
+//   2. after a CTA barrier every warp knows the CTA maximum;
+//   3. only warps whose own maximum equals it search their registers for its lowest index
+//      (normally one warp per CTA), and a second CTA barrier publishes the result;
+//   4. each CTA writes its (maximum, lowest index) into rank 0's shared memory through
+//      distributed shared memory, followed by the one cluster barrier;
+//   5. rank 0 takes the largest maximum and the lowest index among the CTAs holding it
+//      and writes the row's outputs.
 // No atomics, no fences, no workspace. Used for the argmax / gather / shard-key modes when
 // a row needs at most kMaxClusterCtas x kMaxClusterWarps warp segments.
 constexpr int kMaxClusterCtas = 8;
 
-__device__ __forceinline__ unsigned long long warp_min_u64(unsigned long long v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const unsigned long long other = __shfl_xor_sync(kFull, v, o);
-    v = other < v ? other : v;
-  }
-  return v;
-}
-
 // Where row `row` (group-major) and its mask live; bad_state for out-of-range DFA states.
 template <int DT>
-__device__ __forceinline__ void locate_row(const ScanParams& p, int64_t row, const void** base,
+__device__ __forceinline__ void locate_row(const ScanParams& p, uint32_t row, const void** base,
                                            const uint32_t** mrow, bool* bad_state) {
+  // the cluster path never verifies: one row per group
   using St = typename Elem<DT>::storage;
-  const int64_t group = row / p.per_group;
-  const int64_t member = row - group * p.per_group;
+  const int64_t group = row;
+  const int64_t member = 0;
   *base = static_cast<const St*>(p.logits) + group * p.group_stride + member * p.row_stride;
   *mrow = nullptr;
   *bad_state = false;
@@ -666,16 +669,17 @@ template <int DT, int MODE, int MAXWARPS, class Seg>
 __device__ __forceinline__ void cluster_select(const ScanParams& p) {
   namespace cg = cooperative_groups;
   __shared__ unsigned long long s_wmax[MAXWARPS];
-  __shared__ unsigned long long s_cmax[kMaxClusterCtas];  // every CTA's maximum, in every CTA
+  __shared__ unsigned long long s_cmax[kMaxClusterCtas];  // rank 0: every CTA's maximum
   __shared__ uint32_t s_widx[MAXWARPS];
-  __shared__ uint32_t s_cidx[kMaxClusterCtas];  // rank 0: every CTA's lowest index
+  __shared__ uint32_t s_cidx[kMaxClusterCtas];  // rank 0: every CTA's lowest index of it
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int C = p.ctas_per_row;  // cluster size
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int nwarps = blockDim.x >> 5;
-  const int64_t row = blockIdx.x / C;  // one cluster per row
+  uint32_t row;  // one cluster per row
+  asm("mov.u32 %0, %%clusterid.x;" : "=r"(row));
   const int seg_id = rank * nwarps + warp;
   const unsigned long long nan_code = (DT == kF64) ? kOrd64NaN : (unsigned long long)kOrd32NaN;
 
@@ -697,33 +701,35 @@ __device__ __forceinline__ void cluster_select(const ScanParams& p) {
   }
   asm volatile("griddepcontrol.launch_dependents;" :::);
 
-  // 2. row maximum through every CTA's shared memory
+  // 2. CTA maximum, known to every warp after one CTA barrier
   if (lane == 0) s_wmax[warp] = wmax;
   __syncthreads();
-  if (warp == 0) {
-    const unsigned long long cmax = warp_max_u64(lane < nwarps ? s_wmax[lane] : 0ull);
-    if (lane < C) *cluster.map_shared_rank(&s_cmax[rank], lane) = cmax;
-  }
-  cluster.sync();
-  const unsigned long long M = warp_max_u64(lane < C ? s_cmax[lane] : 0ull);
+  const unsigned long long cmax = warp_max_u64(lane < nwarps ? s_wmax[lane] : 0ull);
 
-  // 3. lowest index of the maximum, by the warps that hold it
+  // 3. lowest index of the CTA maximum, searched by the warps that hold it
   uint32_t widx = 0xFFFFFFFFu;
-  if (active && wmax == M && M != 0ull && M != nan_code) widx = seg.first_index(M);
+  if (active && wmax == cmax && cmax != 0ull && cmax != nan_code) widx = seg.first_index(cmax);
   if (lane == 0) s_widx[warp] = widx;
   __syncthreads();
+
+  // 4. each CTA's (maximum, lowest index) into rank 0's shared memory, one cluster barrier
   if (warp == 0) {
     const uint32_t cidx = __reduce_min_sync(kFull, lane < nwarps ? s_widx[lane] : 0xFFFFFFFFu);
-    if (lane == 0) *cluster.map_shared_rank(&s_cidx[rank], 0) = cidx;
+    if (lane == 0) {
+      *cluster.map_shared_rank(&s_cmax[rank], 0) = cmax;
+      *cluster.map_shared_rank(&s_cidx[rank], 0) = cidx;
+    }
   }
   cluster.sync();
 
-  // 4. outputs
+  // 5. outputs: the lowest index among the CTAs holding the row maximum
   if (rank == 0 && warp == 0) {
+    const unsigned long long cm = lane < C ? s_cmax[lane] : 0ull;
+    const unsigned long long M = warp_max_u64(cm);
     Partial part;
     part.flags = (bad_state ? kFlagBadState : 0u) | (M ? kFlagAny : 0u);
     part.ord = M;
-    const uint32_t idx = (uint32_t)warp_min_u64(lane < C ? s_cidx[lane] : 0xFFFFFFFFull);
+    const uint32_t idx = __reduce_min_sync(kFull, (lane < C && cm == M) ? s_cidx[lane] : 0xFFFFFFFFu);
     part.idx = idx == 0xFFFFFFFFu ? idx : idx + (uint32_t)p.idx_offset;
     finalize_group<MODE, DT == kF64>(p, row, &part, lane, 1);
   }
@@ -1042,6 +1048,8 @@ static bool dispatch_cluster(int dt, bool fast, ScanParams& p, cudaStream_t s, b
 
 template <int MODE>
 static cudaError_t dispatch(int dt, bool fast, const ScanParams& p, cudaStream_t s, bool pdl) {
+  // kernels index rows and CTAs in 32 bits; a grid never exceeds rows x segments blocks
+  if (p.rows * (int64_t)p.segs > 0x7FFFFFFFll) return cudaErrorInvalidValue;
   switch (dt) {
     case kBF16:
       return fast ? launch_t<kBF16, true, MODE>(p, s, pdl) : launch_t<kBF16, false, MODE>(p, s, pdl);
