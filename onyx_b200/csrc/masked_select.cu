@@ -173,6 +173,7 @@ struct WarpSegment {
   uint32_t bits[UNROLL];
   uint32_t tail_raw, tail_bit;
   uint32_t tord;  // this lane's maximum as an order code, 0 = no valid token
+  uint32_t vm[(DT == kF32) ? 1 : UNROLL];  // 16-bit types: each vector's masked pair maximum
   uint32_t e0, nv;  // in-row indices are 32-bit: rows are shorter than 2^31 elements
   int lane;
 
@@ -236,7 +237,10 @@ struct WarpSegment {
     } else {
       uint32_t pm = V::kNegInfPair;
 #pragma unroll
-      for (int k = 0; k < UNROLL; ++k) pm = V::pmax(pm, V::masked_pair_max(x[k], bits[k]));
+      for (int k = 0; k < UNROLL; ++k) {
+        vm[k] = V::masked_pair_max(x[k], bits[k]);
+        pm = V::pmax(pm, vm[k]);
+      }
       tmax = V::pair_to_f32_max(pm);
     }
     if (tail_bit) tmax = max_nan_f32(tmax, V::scalar(tail_raw));
@@ -263,8 +267,7 @@ struct WarpSegment {
         m2 = h | (h << 16);
 #pragma unroll
         for (int k = UNROLL - 1; k >= 0; --k)
-          if (bits[k] && V::eq_mask(V::masked_pair_max(x[k], bits[k]), m2))
-            key = ((uint32_t)k << 5) | lane;
+          if (bits[k] && V::eq_mask(vm[k], m2)) key = ((uint32_t)k << 5) | lane;
       }
       if (key == 0xFFFFFFFFu && tail_bit && ord32(V::scalar(tail_raw)) == M)
         key = ((uint32_t)UNROLL << 5) | lane;  // the ragged tail follows every full vector
