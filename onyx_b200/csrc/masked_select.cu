@@ -26,7 +26,6 @@
 #include "onyx_common.cuh"
 #include "../../include/onyx_b200.h"
 
-#include <cooperative_groups.h>
 
 #include <algorithm>
 #include <cstdlib>
@@ -646,95 +645,108 @@ __global__ void __launch_bounds__(MAXWARPS * 32)
 // a row needs at most kMaxClusterCtas x kMaxClusterWarps warp segments.
 constexpr int kMaxClusterCtas = 8;
 
-// Where row `row` (group-major) and its mask live; bad_state for out-of-range DFA states.
+// Whether row `row`'s DFA state id (gather mode) lies outside the table.
+__device__ __forceinline__ bool row_bad_state(const ScanParams& p, uint32_t row) {
+  if (!p.mask || !p.state_ids) return false;
+  const int32_t s = __ldg(p.state_ids + row);
+  return (s < 0) || ((int64_t)s >= p.n_states);
+}
+
+// Where row `row` and its mask live (one row per group: the cluster path never verifies);
+// nullptr logits for a row whose DFA state id is out of range.
 template <int DT>
 __device__ __forceinline__ void locate_row(const ScanParams& p, uint32_t row, const void** base,
-                                           const uint32_t** mrow, bool* bad_state) {
-  // the cluster path never verifies: one row per group
+                                           const uint32_t** mrow) {
   using St = typename Elem<DT>::storage;
-  const int64_t group = row;
-  const int64_t member = 0;
-  *base = static_cast<const St*>(p.logits) + group * p.group_stride + member * p.row_stride;
+  *base = static_cast<const St*>(p.logits) + (int64_t)row * p.group_stride;
   *mrow = nullptr;
-  *bad_state = false;
   if (p.mask) {
     if (p.state_ids) {
       const int32_t s = __ldg(p.state_ids + row);
-      *bad_state = (s < 0) || ((int64_t)s >= p.n_states);
-      *mrow = p.mask + (*bad_state ? 0 : (int64_t)s * p.mask_row_stride);
+      if ((s < 0) || ((int64_t)s >= p.n_states)) {
+        *base = nullptr;
+      } else {
+        *mrow = p.mask + (int64_t)s * p.mask_row_stride;
+      }
     } else {
-      *mrow = p.mask + group * p.mask_group_stride + member * p.mask_row_stride;
+      *mrow = p.mask + (int64_t)row * p.mask_group_stride;
     }
   }
 }
 
 template <int DT, int MODE, int MAXWARPS, class Seg>
 __device__ __forceinline__ void cluster_select(const ScanParams& p) {
-  namespace cg = cooperative_groups;
-  __shared__ unsigned long long s_wmax[MAXWARPS];
-  __shared__ unsigned long long s_cmax[kMaxClusterCtas];  // rank 0: every CTA's maximum
+  static_assert(DT != kF64, "f64 order codes do not pack with an index");
+  __shared__ uint32_t s_wmax[MAXWARPS];
   __shared__ uint32_t s_widx[MAXWARPS];
-  __shared__ uint32_t s_cidx[kMaxClusterCtas];  // rank 0: every CTA's lowest index of it
-  cg::cluster_group cluster = cg::this_cluster();
-  const int rank = (int)cluster.block_rank();
-  const int C = p.ctas_per_row;  // cluster size
+  __shared__ unsigned long long s_key[kMaxClusterCtas];  // rank 0: every CTA's key
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int nwarps = blockDim.x >> 5;
-  uint32_t row;  // one cluster per row
+  uint32_t rank, row;  // one cluster per row
+  asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
   asm("mov.u32 %0, %%clusterid.x;" : "=r"(row));
-  const int seg_id = rank * nwarps + warp;
-  const unsigned long long nan_code = (DT == kF64) ? kOrd64NaN : (unsigned long long)kOrd32NaN;
+  const int C = p.ctas_per_row;  // cluster size
+  const int seg_id = (int)rank * nwarps + warp;
 
+  // First phase of the cluster barrier: its completion, awaited just before the first
+  // access to another CTA's shared memory, guarantees every CTA of the cluster is running.
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   const void* row_base;
   const uint32_t* mrow;
-  bool bad_state;
-  locate_row<DT>(p, row, &row_base, &mrow, &bad_state);
+  locate_row<DT>(p, row, &row_base, &mrow);
 
   // 1. segment maximum
   Seg seg;
-  const bool active = !bad_state && seg_id < p.segs;  // warp-uniform
-  unsigned long long wmax = 0ull;
+  const bool active = row_base != nullptr && seg_id < p.segs;  // warp-uniform
+  uint32_t wmax = 0u;
   if (active) {
     const int64_t e0 = (int64_t)seg_id * p.seg_elems;
     seg.load(row_base, mrow, e0, min(e0 + p.seg_elems, p.vocab), lane);
-    wmax = (unsigned long long)seg.max_code();
+    wmax = (uint32_t)seg.max_code();
   }
   asm volatile("griddepcontrol.launch_dependents;" :::);
 
   // 2. CTA maximum, known to every warp after one CTA barrier
   if (lane == 0) s_wmax[warp] = wmax;
   __syncthreads();
-  const unsigned long long cmax = warp_max_u64(lane < nwarps ? s_wmax[lane] : 0ull);
+  const uint32_t cmax = __reduce_max_sync(kFull, lane < nwarps ? s_wmax[lane] : 0u);
 
   // 3. lowest index of the CTA maximum, searched by the warps that hold it
   uint32_t widx = 0xFFFFFFFFu;
-  if (active && wmax == cmax && cmax != 0ull && cmax != nan_code) widx = seg.first_index(cmax);
+  if (active && wmax == cmax && cmax != 0u && cmax != kOrd32NaN) widx = seg.first_index(cmax);
   if (lane == 0) s_widx[warp] = widx;
   __syncthreads();
 
-  // 4. each CTA's (maximum, lowest index) into rank 0's shared memory, one cluster barrier
+  // 4. each CTA's key (maximum << 32 | ~lowest index) into rank 0's shared memory, then
+  //    the second phase of the cluster barrier
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
   if (warp == 0) {
     const uint32_t cidx = __reduce_min_sync(kFull, lane < nwarps ? s_widx[lane] : 0xFFFFFFFFu);
     if (lane == 0) {
-      *cluster.map_shared_rank(&s_cmax[rank], 0) = cmax;
-      *cluster.map_shared_rank(&s_cidx[rank], 0) = cidx;
+      const unsigned long long key = ((unsigned long long)cmax << 32) | (0xFFFFFFFFu - cidx);
+      const uint32_t local = (uint32_t)__cvta_generic_to_shared(&s_key[rank]);
+      uint32_t remote;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(remote) : "r"(local));
+      asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(remote), "l"(key) : "memory");
     }
   }
-  cluster.sync();
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 
-  // 5. outputs: the lowest index among the CTAs holding the row maximum
+  // 5. outputs: the largest key among the CTAs is the row maximum at its lowest index
   if (rank == 0 && warp == 0) {
-    const unsigned long long cm = lane < C ? s_cmax[lane] : 0ull;
-    const unsigned long long M = warp_max_u64(cm);
+    const unsigned long long key = lane < C ? s_key[lane] : 0ull;
+    const uint32_t M = __reduce_max_sync(kFull, (uint32_t)(key >> 32));
+    const uint32_t low = __reduce_max_sync(kFull, (uint32_t)(key >> 32) == M ? (uint32_t)key : 0u);
+    const uint32_t idx = 0xFFFFFFFFu - low;
     Partial part;
-    part.flags = (bad_state ? kFlagBadState : 0u) | (M ? kFlagAny : 0u);
+    part.flags = (row_bad_state(p, row) ? kFlagBadState : 0u) | (M ? kFlagAny : 0u);
     part.ord = M;
-    const uint32_t idx = __reduce_min_sync(kFull, (lane < C && cm == M) ? s_cidx[lane] : 0xFFFFFFFFu);
     part.idx = idx == 0xFFFFFFFFu ? idx : idx + (uint32_t)p.idx_offset;
-    finalize_group<MODE, DT == kF64>(p, row, &part, lane, 1);
+    finalize_group<MODE, false>(p, row, &part, lane, 1);
   }
 }
 
@@ -1023,7 +1035,9 @@ static bool dispatch_cluster(int dt, bool fast, ScanParams& p, cudaStream_t s, b
     int ctas = 0, warps = 0;
     if (!cluster_enabled() || p.per_group != 1 || !cluster_layout(p.segs, &ctas, &warps))
       return false;
-    if (dt == kF64 && MODE == kModeKey) return false;
+    // f64 order codes are 64-bit and do not pack with an index: the ticket merge serves it
+    if (dt == kF64) return false;
+    if (p.rows * (int64_t)ctas > 0x7FFFFFFFll) return false;
     p.ctas_per_row = ctas;
     switch (dt) {
       case kBF16:
@@ -1038,12 +1052,6 @@ static bool dispatch_cluster(int dt, bool fast, ScanParams& p, cudaStream_t s, b
         *err = fast ? launch_cluster_t<kF32, true, MODE>(p, warps, s, pdl)
                     : launch_cluster_t<kF32, false, MODE>(p, warps, s, pdl);
         return true;
-      case kF64:
-        if constexpr (MODE != kModeKey) {
-          *err = launch_cluster_t<kF64, false, MODE>(p, warps, s, pdl);
-          return true;
-        }
-        return false;
     }
     return false;
   }
