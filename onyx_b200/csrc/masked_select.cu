@@ -539,6 +539,45 @@ __device__ void finalize_group(const ScanParams& p, int64_t group, const Partial
   }
 }
 
+// Speculative-verify outputs of one group whose rows left one partial each (the cluster
+// path), for groups of at most 32 rows: lane i reads row i's partial and draft token, so
+// all rows are read in one round trip, and ballots find the first row that decides. Same
+// decisions as finalize_group's member loop; the partials are zeroed after reading.
+template <bool IS64>
+__device__ void finalize_verify_rows(const ScanParams& p, uint32_t group, int lane) {
+  const int P = p.per_group, G = P - 1;
+  Partial* base = p.ws_part + (int64_t)group * P;
+  Partial r = empty_partial();
+  int32_t draft = 0;
+  if (lane < P) {
+    r = ld_partial_cg(base + lane);
+    __stcg(reinterpret_cast<ulonglong2*>(base + lane), make_ulonglong2(0ull, 0ull));
+    if (lane < G) draft = __ldg(p.drafts + (int64_t)group * p.draft_stride + lane);
+  }
+  int32_t sel = -1;
+  uint32_t rs = 0u;
+  if (lane < P) decode_partial(r, IS64, &sel, &rs);
+  // first draft position whose row carries a status or selects another token
+  const unsigned miss = __ballot_sync(kFull, lane < G && (rs != 0u || sel != draft));
+  const int acc = miss ? __ffs(miss) - 1 : G;
+  const int32_t sel_d = __shfl_sync(kFull, sel, acc);
+  const uint32_t rs_d = __shfl_sync(kFull, rs, acc);
+  if (lane == 0) {
+    int32_t corr = -1;
+    uint32_t st = 0u;
+    if (acc < G || p.bonus) {  // a mismatch's replacement, or the bonus from row G
+      if (rs_d) {
+        st = rs_d;
+      } else {
+        corr = sel_d;
+      }
+    }
+    p.accept_len[group] = acc;
+    p.correction[group] = corr;
+    p.out_status[group] = st;
+  }
+}
+
 // Release the warp's partial and take a ticket; true for the warp that completes a group.
 __device__ __forceinline__ bool take_ticket(Partial* slot, const Partial& part, uint32_t* counter,
                                             uint32_t total, int lane) {
@@ -652,12 +691,20 @@ __device__ __forceinline__ bool row_bad_state(const ScanParams& p, uint32_t row)
   return (s < 0) || ((int64_t)s >= p.n_states);
 }
 
-// Where row `row` and its mask live (one row per group: the cluster path never verifies);
-// nullptr logits for a row whose DFA state id is out of range.
-template <int DT>
+// Where row `row` and its mask live; nullptr logits for a row whose DFA state id is out
+// of range. Rows are group-major; groups hold more than one row only when verifying.
+template <int DT, int MODE>
 __device__ __forceinline__ void locate_row(const ScanParams& p, uint32_t row, const void** base,
                                            const uint32_t** mrow) {
   using St = typename Elem<DT>::storage;
+  if constexpr (MODE == kModeVerify) {
+    const uint32_t group = row / (uint32_t)p.per_group;
+    const uint32_t member = row - group * (uint32_t)p.per_group;
+    *base = static_cast<const St*>(p.logits) + (int64_t)group * p.group_stride +
+            (int64_t)member * p.row_stride;
+    *mrow = p.mask + (int64_t)group * p.mask_group_stride + (int64_t)member * p.mask_row_stride;
+    return;
+  }
   *base = static_cast<const St*>(p.logits) + (int64_t)row * p.group_stride;
   *mrow = nullptr;
   if (p.mask) {
@@ -696,7 +743,7 @@ __device__ __forceinline__ void cluster_select(const ScanParams& p) {
 
   const void* row_base;
   const uint32_t* mrow;
-  locate_row<DT>(p, row, &row_base, &mrow);
+  locate_row<DT, MODE>(p, row, &row_base, &mrow);
 
   // 1. segment maximum
   Seg seg;
@@ -746,14 +793,26 @@ __device__ __forceinline__ void cluster_select(const ScanParams& p) {
     part.flags = (row_bad_state(p, row) ? kFlagBadState : 0u) | (M ? kFlagAny : 0u);
     part.ord = M;
     part.idx = idx == 0xFFFFFFFFu ? idx : idx + (uint32_t)p.idx_offset;
-    finalize_group<MODE, false>(p, row, &part, lane, 1);
+    if constexpr (MODE == kModeVerify) {
+      // the row's result joins its group through one ticket per row; the last row of the
+      // group decides acceptance
+      const uint32_t group = row / (uint32_t)p.per_group;
+      if (take_ticket(p.ws_part + row, part, p.ws_count + group, (uint32_t)p.per_group, lane)) {
+        if (p.per_group <= 32) {
+          finalize_verify_rows<false>(p, group, lane);
+        } else {
+          finalize_group<MODE, false>(p, group, nullptr, lane, 1);
+        }
+      }
+    } else {
+      finalize_group<MODE, false>(p, row, &part, lane, 1);
+    }
   }
 }
 
 template <int DT, bool FAST, int MODE, int MAXWARPS, int UNROLL>
 __global__ void __launch_bounds__(MAXWARPS * 32, 1024 / (MAXWARPS * 32))
     masked_select_cluster_kernel(const ScanParams p) {
-  static_assert(MODE != kModeVerify, "verify groups span several rows");
   if constexpr (FAST) {
     cluster_select<DT, MODE, MAXWARPS, WarpSegment<DT, UNROLL>>(p);
   } else {
@@ -1029,11 +1088,10 @@ static cudaError_t launch_cluster_t(const ScanParams& p, int warps, cudaStream_t
 template <int MODE>
 static bool dispatch_cluster(int dt, bool fast, ScanParams& p, cudaStream_t s, bool pdl,
                              cudaError_t* err) {
-  if constexpr (MODE == kModeVerify) {
-    return false;
-  } else {
+  {
     int ctas = 0, warps = 0;
-    if (!cluster_enabled() || p.per_group != 1 || !cluster_layout(p.segs, &ctas, &warps))
+    if (!cluster_enabled() || (MODE != kModeVerify && p.per_group != 1) ||
+        !cluster_layout(p.segs, &ctas, &warps))
       return false;
     // f64 order codes are 64-bit and do not pack with an index: the ticket merge serves it
     if (dt == kF64) return false;
@@ -1278,11 +1336,15 @@ int onyx_spec_verify(const void* logits, int dtype, int64_t batch, int64_t gamma
   p.bonus = bonus ? 1 : 0;
   p.accept_len = accept_len;
   p.correction = correction;
-  // verify grids span several waves; the all-ticket merge measured faster there than one
-  // cluster per row
   const int rc = bind_workspace(p, workspace, workspace_bytes,
                                 workspace_bytes_for(p.rows, batch, pl, P), batch);
   if (rc) return rc;
+  // one cluster per row, rows joined per group by a ticket; uses the first `rows`
+  // partials of the workspace bound above for the ticket layout
+  cudaError_t cluster_err = cudaSuccess;
+  if (dispatch_cluster<kModeVerify>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled(),
+                                    &cluster_err))
+    return finish_launch(cluster_err);
   return finish_launch(dispatch<kModeVerify>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled()));
 }
 
