@@ -93,8 +93,7 @@ struct Packed16 {
   // masked maximum of one vector (8 mask bits in `bits`), as a packed pair
   __device__ static uint32_t masked_pair_max(const uint4& x, uint32_t bits) {
     uint32_t m01, m23, m45, m67;
-    expand4_16(bits, m01, m23);
-    expand4_16(bits >> 4, m45, m67);
+    expand8_16(bits, m01, m23, m45, m67);
     const uint32_t a0 = (x.x & m01) | (kNegInfPair & ~m01);
     const uint32_t a1 = (x.y & m23) | (kNegInfPair & ~m23);
     const uint32_t a2 = (x.z & m45) | (kNegInfPair & ~m45);
@@ -218,16 +217,19 @@ struct WarpSegment {
       }
       tail_bit = mrow ? ((__ldg(mrow + (te >> 5)) >> (te & 31)) & 1u) : 1u;
     }
+    // the lane's mask bits in the low bits; higher bits (other lanes') are ignored by
+    // every consumer
     const uint32_t lane_shift = (uint32_t)(lane * E) & 31u;
 #pragma unroll
-    for (int k = 0; k < UNROLL; ++k) bits[k] = (w[k] >> lane_shift) & kLaneBits;
+    for (int k = 0; k < UNROLL; ++k) bits[k] = w[k] >> lane_shift;
   }
 
   // warp maximum as an order code (0: no valid token in the segment)
   __device__ __forceinline__ uint32_t max_code() {
-    uint32_t any = tail_bit;
+    uint32_t any = 0u;
 #pragma unroll
     for (int k = 0; k < UNROLL; ++k) any |= bits[k];
+    any = (any & kLaneBits) | tail_bit;
     float tmax;
     if constexpr (DT == kF32) {
       tmax = __int_as_float(0xFF800000);
@@ -260,13 +262,14 @@ struct WarpSegment {
       if constexpr (DT == kF32) {
 #pragma unroll
         for (int k = UNROLL - 1; k >= 0; --k)
-          if (bits[k] && V::masked_max(x[k], bits[k]) == mf) key = ((uint32_t)k << 5) | lane;
+          if ((bits[k] & kLaneBits) && V::masked_max(x[k], bits[k]) == mf)
+            key = ((uint32_t)k << 5) | lane;
       } else {
         const uint32_t h = V::from_f32(mf);
         m2 = h | (h << 16);
 #pragma unroll
         for (int k = UNROLL - 1; k >= 0; --k)
-          if (bits[k] && V::eq_mask(vm[k], m2)) key = ((uint32_t)k << 5) | lane;
+          if ((bits[k] & kLaneBits) && V::eq_mask(vm[k], m2)) key = ((uint32_t)k << 5) | lane;
       }
       if (key == 0xFFFFFFFFu && tail_bit && ord32(V::scalar(tail_raw)) == M)
         key = ((uint32_t)UNROLL << 5) | lane;  // the ragged tail follows every full vector
@@ -293,8 +296,7 @@ struct WarpSegment {
       const uint32_t h = V::from_f32(mf);
       m2 = h | (h << 16);
       uint32_t m01, m23, m45, m67;
-      expand4_16(bv, m01, m23);
-      expand4_16(bv >> 4, m45, m67);
+      expand8_16(bv, m01, m23, m45, m67);
       // element j of the vector owns 16-bit lane j of the 64-bit words q (j < 4), r
       const uint32_t q0 = V::eq_mask(xv.x, m2) & m01;
       const uint32_t q1 = V::eq_mask(xv.y, m2) & m23;
@@ -852,8 +854,7 @@ __device__ __forceinline__ uint4 apply_vec(const uint4& x, uint32_t bits, uint32
   if constexpr (DT == kBF16 || DT == kF16) {
     constexpr uint32_t n = (DT == kBF16) ? 0xFF80FF80u : 0xFC00FC00u;
     uint32_t m01, m23, m45, m67;
-    expand4_16(bits, m01, m23);
-    expand4_16(bits >> 4, m45, m67);
+    expand8_16(bits, m01, m23, m45, m67);
     o.x = (x.x & m01) | (n & ~m01);
     o.y = (x.y & m23) | (n & ~m23);
     o.z = (x.z & m45) | (n & ~m45);

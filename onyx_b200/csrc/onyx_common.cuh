@@ -138,14 +138,21 @@ __device__ __forceinline__ uint32_t prmt_sign(uint32_t a, uint32_t sel) {
   return d;
 }
 
-// Expand 4 mask bits (b0..b3) into per-16-bit-lane masks for two packed registers:
-// m01 = [b0 b0 b1 b1] bytes, m23 = [b2 b2 b3 b3] bytes (0x00 or 0xFF each).
-// The multiply moves bit k to bit 8k+7 without carries; prmt then sign-replicates the
-// selected bytes.
-__device__ __forceinline__ void expand4_16(uint32_t nib, uint32_t& m01, uint32_t& m23) {
-  const uint32_t s = (nib & 0xFu) * 0x10204080u;
-  m01 = prmt_sign(s, 0x9988u);
-  m23 = prmt_sign(s, 0xBBAAu);
+// Expand the 8 mask bits b0..b7 in the low byte of `bits` (higher bits ignored) into
+// per-16-bit-lane masks for four packed registers: m01 = [b0 b0 b1 b1] bytes, m23 =
+// [b2 b2 b3 b3], m45 = [b4 b4 b5 b5], m67 = [b6 b6 b7 b7] (0x00 or 0xFF each). Bit i
+// (i = 0..3) times 0x10204080 has terms at bits i+7, i+14, i+21, i+28, and bit 4+i times
+// 0x01020408 at 7+i, 14+i, 21+i, 28+i: in each product the sixteen positions are distinct,
+// so nothing carries, and bits 7, 15, 23, 31 hold b0..b3 (b4..b7: the high nibble needs no
+// shift first). prmt then sign-replicates the selected bytes.
+__device__ __forceinline__ void expand8_16(uint32_t bits, uint32_t& m01, uint32_t& m23,
+                                           uint32_t& m45, uint32_t& m67) {
+  const uint32_t lo = (bits & 0x0Fu) * 0x10204080u;
+  const uint32_t hi = (bits & 0xF0u) * 0x01020408u;
+  m01 = prmt_sign(lo, 0x9988u);
+  m23 = prmt_sign(lo, 0xBBAAu);
+  m45 = prmt_sign(hi, 0x9988u);
+  m67 = prmt_sign(hi, 0xBBAAu);
 }
 
 // 16-bit float helpers (bit pattern -> float)

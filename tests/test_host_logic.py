@@ -151,3 +151,33 @@ def test_workload_shapes_and_determinism():
     v = workloads.synthetic_vocabulary(np.random.default_rng(1), 1000)
     assert len(v) == 1000 and all(len(t) == 1 for t in v[:256])
     assert all(2 <= len(t) <= 8 and all(0x20 <= c < 0x7F for c in t) for t in v[256:])
+
+
+def _prmt_sign(word: int, sel: int) -> int:
+    """prmt.b32 d, word, 0, sel with every selector nibble in sign-replicate mode: byte n of
+    d is 0xFF when bit 7 of byte (nibble n & 3) of `word` is set, else 0x00."""
+    out = 0
+    for n in range(4):
+        src = (sel >> (4 * n)) & 0x3
+        if (word >> (8 * src + 7)) & 1:
+            out |= 0xFF << (8 * n)
+    return out
+
+
+def test_mask_expansion_multiplies_are_carry_free():
+    """The device expansion of 8 mask bits into four packed 16-bit lane masks
+    (expand8_16 in onyx_common.cuh) for every byte value, with the unmasked high bits a
+    shifted mask word leaves above the byte."""
+    for byte in range(256):
+        for above in (0, 0xABCDEF00, 0xFFFFFF00):
+            bits = byte | above
+            lo = ((bits & 0x0F) * 0x10204080) & 0xFFFFFFFF
+            hi = ((bits & 0xF0) * 0x01020408) & 0xFFFFFFFF
+            got = [_prmt_sign(lo, 0x9988), _prmt_sign(lo, 0xBBAA),
+                   _prmt_sign(hi, 0x9988), _prmt_sign(hi, 0xBBAA)]
+            want = []
+            for pair in range(4):
+                b0 = (byte >> (2 * pair)) & 1
+                b1 = (byte >> (2 * pair + 1)) & 1
+                want.append((0xFFFF if b0 else 0) | (0xFFFF0000 if b1 else 0))
+            assert got == want, (byte, above)
