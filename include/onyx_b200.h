@@ -65,6 +65,9 @@ extern "C" {
 #define ONYX_STATUS_NAN_IN_SUPPORT 4u /* a valid value is NaN: rejected by
                                          torch_backend.py:991-996 */
 #define ONYX_STATUS_BAD_STATE 8u      /* gather: DFA state id outside the table */
+#define ONYX_STATUS_WAIT_TIMEOUT 16u  /* a bounded wait inside the kernel for the row's
+                                         partial results gave up (a hardware fault): the
+                                         row's output is not valid */
 
 ONYX_API int onyx_abi_version(void);
 ONYX_API const char* onyx_error_string(int code);

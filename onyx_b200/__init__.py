@@ -20,6 +20,7 @@ from .masked_selection import (
     STATUS_BAD_STATE,
     STATUS_EMPTY_MASK,
     STATUS_NAN_IN_SUPPORT,
+    STATUS_WAIT_TIMEOUT,
     MaskedArgmaxResult,
     SpecVerifyResult,
     combine_partial_keys,
@@ -53,4 +54,5 @@ __all__ = [
     "STATUS_ALL_NEG_INF",
     "STATUS_NAN_IN_SUPPORT",
     "STATUS_BAD_STATE",
+    "STATUS_WAIT_TIMEOUT",
 ]

@@ -30,6 +30,7 @@ STATUS_EMPTY_MASK = 1
 STATUS_ALL_NEG_INF = 2
 STATUS_NAN_IN_SUPPORT = 4
 STATUS_BAD_STATE = 8
+STATUS_WAIT_TIMEOUT = 16
 
 # every symbol include/onyx_b200.h declares, with its ctypes signature
 _i64, _i32, _vp, _sz = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t

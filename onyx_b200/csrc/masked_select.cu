@@ -499,6 +499,7 @@ __device__ void finalize_group(const ScanParams& p, int64_t group, const Partial
     } else {
       unsigned long long key = 0ull;
       if (r.flags & kFlagAny) key = (r.ord << 32) | (unsigned long long)(0xFFFFFFFFu - r.idx);
+      if (r.flags & kFlagWaitTimeout) key = kKeyWaitTimeout;
       p.out_key[group] = key;
     }
   } else {
@@ -686,6 +687,70 @@ __global__ void __launch_bounds__(MAXWARPS * 32)
 // a row needs at most kMaxClusterCtas x kMaxClusterWarps warp segments.
 constexpr int kMaxClusterCtas = 8;
 
+// ---- mbarrier helpers (cluster path) ---------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
+                   smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(unsigned long long* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0u;
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for phase `parity` of `bar` to complete; gives up (false) after `limit_ns`.
+__device__ __noinline__ bool mbar_wait_cluster_bounded(unsigned long long* bar, uint32_t parity,
+                                                       unsigned long long limit_ns) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait_cluster(bar, parity))
+    if (global_ns() - t0 > limit_ns) return false;
+  return true;
+}
+
+// Asynchronous 8-byte store into another CTA's shared memory (both addresses from mapa, in
+// the same CTA) whose completion is counted on that CTA's mbarrier.
+__device__ __forceinline__ void st_async_u64(uint32_t remote_addr, unsigned long long v,
+                                             uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.u64 [%0], %1, [%2];" ::"r"(
+          remote_addr),
+      "l"(v), "r"(remote_bar)
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
+  return r;
+}
+
+constexpr unsigned long long kClusterWaitLimitNs = 500ull * 1000ull * 1000ull;  // 0.5 s
+
 // Whether row `row`'s DFA state id (gather mode) lies outside the table.
 __device__ __forceinline__ bool row_bad_state(const ScanParams& p, uint32_t row) {
   if (!p.mask || !p.state_ids) return false;
@@ -729,6 +794,7 @@ __device__ __forceinline__ void cluster_select(const ScanParams& p) {
   __shared__ uint32_t s_wmax[MAXWARPS];
   __shared__ uint32_t s_widx[MAXWARPS];
   __shared__ unsigned long long s_key[kMaxClusterCtas];  // rank 0: every CTA's key
+  __shared__ unsigned long long s_keys_bar;  // rank 0: completes once every key has landed
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int nwarps = blockDim.x >> 5;
@@ -738,8 +804,14 @@ __device__ __forceinline__ void cluster_select(const ScanParams& p) {
   const int C = p.ctas_per_row;  // cluster size
   const int seg_id = (int)rank * nwarps + warp;
 
+  if (rank == 0 && threadIdx.x == 0) {
+    mbar_init(&s_keys_bar, 1u);  // rank 0's own arrive, plus the other CTAs' key bytes
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncwarp();
   // First phase of the cluster barrier: its completion, awaited just before the first
-  // access to another CTA's shared memory, guarantees every CTA of the cluster is running.
+  // access to another CTA's shared memory, guarantees every CTA of the cluster is running
+  // and rank 0's mbarrier is initialised.
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
@@ -769,30 +841,38 @@ __device__ __forceinline__ void cluster_select(const ScanParams& p) {
   if (lane == 0) s_widx[warp] = widx;
   __syncthreads();
 
-  // 4. each CTA's key (maximum << 32 | ~lowest index) into rank 0's shared memory, then
-  //    the second phase of the cluster barrier
+  // 4. each CTA's key (maximum << 32 | ~lowest index) into rank 0's shared memory: rank 0
+  //    stores its own; every other CTA stores asynchronously, the store's completion counted
+  //    on rank 0's mbarrier, which completes once every key has landed
   asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
   if (warp == 0) {
     const uint32_t cidx = __reduce_min_sync(kFull, lane < nwarps ? s_widx[lane] : 0xFFFFFFFFu);
     if (lane == 0) {
       const unsigned long long key = ((unsigned long long)cmax << 32) | (0xFFFFFFFFu - cidx);
-      const uint32_t local = (uint32_t)__cvta_generic_to_shared(&s_key[rank]);
-      uint32_t remote;
-      asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(remote) : "r"(local));
-      asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(remote), "l"(key) : "memory");
+      if (rank == 0) {
+        s_key[0] = key;
+        mbar_arrive_expect_tx(&s_keys_bar, (uint32_t)(C - 1) * 8u);
+      } else {
+        st_async_u64(map_to_rank(&s_key[rank], 0u), key, map_to_rank(&s_keys_bar, 0u));
+      }
     }
   }
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 
   // 5. outputs: the largest key among the CTAs is the row maximum at its lowest index
+  bool keys_landed = true;
+  if (rank == 0 && warp == 0)
+    keys_landed = __all_sync(kFull, mbar_wait_cluster_bounded(&s_keys_bar, 0u, kClusterWaitLimitNs));
+  // Second phase of the cluster barrier: keeps the other CTAs running until rank 0 holds
+  // their keys.
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   if (rank == 0 && warp == 0) {
     const unsigned long long key = lane < C ? s_key[lane] : 0ull;
     const uint32_t M = __reduce_max_sync(kFull, (uint32_t)(key >> 32));
     const uint32_t low = __reduce_max_sync(kFull, (uint32_t)(key >> 32) == M ? (uint32_t)key : 0u);
     const uint32_t idx = 0xFFFFFFFFu - low;
     Partial part;
-    part.flags = (row_bad_state(p, row) ? kFlagBadState : 0u) | (M ? kFlagAny : 0u);
+    part.flags = (row_bad_state(p, row) ? kFlagBadState : 0u) | (M ? kFlagAny : 0u) |
+                 (keys_landed ? 0u : kFlagWaitTimeout);
     part.ord = M;
     part.idx = idx == 0xFFFFFFFFu ? idx : idx + (uint32_t)p.idx_offset;
     if constexpr (MODE == kModeVerify) {
@@ -810,6 +890,7 @@ __device__ __forceinline__ void cluster_select(const ScanParams& p) {
       finalize_group<MODE, false>(p, row, &part, lane, 1);
     }
   }
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
 }
 
 template <int DT, bool FAST, int MODE, int MAXWARPS, int UNROLL>
@@ -975,7 +1056,7 @@ __global__ void combine_keys_kernel(const unsigned long long* keys, int64_t n_pa
     best = k > best ? k : best;
   }
   Partial pr;
-  pr.flags = best ? kFlagAny : 0u;
+  pr.flags = (best == kKeyWaitTimeout ? kFlagWaitTimeout : 0u) | (best ? kFlagAny : 0u);
   pr.ord = best >> 32;
   pr.idx = 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull);
   decode_partial(pr, false, &out_idx[r], &out_status[r]);

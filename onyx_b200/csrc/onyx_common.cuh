@@ -29,11 +29,16 @@ constexpr uint32_t kStatusEmptyMask = 1u;
 constexpr uint32_t kStatusAllNegInf = 2u;
 constexpr uint32_t kStatusNanInSupport = 4u;
 constexpr uint32_t kStatusBadState = 8u;
+constexpr uint32_t kStatusWaitTimeout = 16u;
 
 // partial-result flags
 constexpr uint32_t kFlagAny = 1u;        // the segment holds at least one valid token
 constexpr uint32_t kFlagBadState = 2u;   // the DFA state id of the row is out of range
 constexpr uint32_t kFlagAboveNegInf = 4u;  // some valid value is not -inf (mask apply)
+constexpr uint32_t kFlagWaitTimeout = 8u;  // a bounded wait for the row's partials gave up
+// shard key of a row whose bounded wait gave up: above every real key (a NaN maximum has
+// low word 0), so it wins every combine
+constexpr unsigned long long kKeyWaitTimeout = ~0ull;
 
 constexpr uint32_t kOrd32NaN = 0xFFFFFFFFu;
 constexpr uint32_t kOrd32NegInf = 0x007FFFFFu;  // ord32(-inf)
@@ -73,6 +78,11 @@ __device__ __forceinline__ bool better(unsigned long long ord_a, uint32_t idx_a,
 // Decode a row's combined partial into (index, status).
 __device__ __forceinline__ void decode_partial(const Partial& p, bool is64, int32_t* idx,
                                                uint32_t* status) {
+  if (p.flags & kFlagWaitTimeout) {
+    *idx = -1;
+    *status = kStatusWaitTimeout;
+    return;
+  }
   if (p.flags & kFlagBadState) {
     *idx = -1;
     *status = kStatusBadState;

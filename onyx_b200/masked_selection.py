@@ -42,12 +42,14 @@ __all__ = [
     "STATUS_ALL_NEG_INF",
     "STATUS_NAN_IN_SUPPORT",
     "STATUS_BAD_STATE",
+    "STATUS_WAIT_TIMEOUT",
 ]
 
 STATUS_EMPTY_MASK = _lib.STATUS_EMPTY_MASK
 STATUS_ALL_NEG_INF = _lib.STATUS_ALL_NEG_INF
 STATUS_NAN_IN_SUPPORT = _lib.STATUS_NAN_IN_SUPPORT
 STATUS_BAD_STATE = _lib.STATUS_BAD_STATE
+STATUS_WAIT_TIMEOUT = _lib.STATUS_WAIT_TIMEOUT
 
 _DTYPE_CODES = {
     torch.float32: _lib.DTYPE_F32,

@@ -60,6 +60,8 @@ def _read_selection(result: _ms.MaskedArgmaxResult, vocab: int, *, masked: bool)
     except Exception as exc:
         raise TorchBackendExecutionError(f"CUDA argmax failed: {exc}") from exc
     selected, status = int(both[0, 0]), int(both[1, 0])
+    if status & _ms.STATUS_WAIT_TIMEOUT:
+        raise TorchBackendExecutionError("CUDA argmax failed: a bounded in-kernel wait gave up")
     if status & _ms.STATUS_NAN_IN_SUPPORT:
         raise TorchBackendInvariantError("CUDA logits cannot contain NaN")
     if masked and status & _ms.STATUS_EMPTY_MASK:

@@ -86,6 +86,9 @@ def combine_keys_host(keys_by_shard: list[list[int]]) -> list[tuple[int, int]]:
         if best == 0:
             out.append((-1, _ms.STATUS_EMPTY_MASK))
             continue
+        if best == _MASK64:  # a shard whose in-kernel wait gave up
+            out.append((-1, _ms.STATUS_WAIT_TIMEOUT))
+            continue
         order = best >> 32
         if order == 0xFFFFFFFF:
             out.append((-1, _ms.STATUS_NAN_IN_SUPPORT))
