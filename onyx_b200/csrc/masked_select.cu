@@ -67,6 +67,9 @@ struct ScanParams {
   int bonus;
   int32_t* accept_len;
   int32_t* correction;
+  // test hook: key bytes rank 0 of the cluster path expects beyond those sent (0 normally;
+  // nonzero makes its bounded wait run out)
+  uint32_t withheld_key_bytes;
 };
 
 constexpr int kMaxPerGroup = 256;
@@ -851,7 +854,7 @@ __device__ __forceinline__ void cluster_select(const ScanParams& p) {
       const unsigned long long key = ((unsigned long long)cmax << 32) | (0xFFFFFFFFu - cidx);
       if (rank == 0) {
         s_key[0] = key;
-        mbar_arrive_expect_tx(&s_keys_bar, (uint32_t)(C - 1) * 8u);
+        mbar_arrive_expect_tx(&s_keys_bar, (uint32_t)(C - 1) * 8u + p.withheld_key_bytes);
       } else {
         st_async_u64(map_to_rank(&s_key[rank], 0u), key, map_to_rank(&s_keys_bar, 0u));
       }
@@ -1141,6 +1144,12 @@ static bool cluster_layout(int segs, int* ctas, int* warps) {
   return true;
 }
 
+// Test hook for the cluster path's bounded wait (ONYX_B200_TEST_WITHHELD_KEY_BYTES).
+static uint32_t withheld_key_bytes() {
+  const char* v = getenv("ONYX_B200_TEST_WITHHELD_KEY_BYTES");
+  return v ? (uint32_t)strtoul(v, nullptr, 10) & 0xFFFFu : 0u;
+}
+
 static bool cluster_enabled() {
   const char* v = getenv("ONYX_B200_CLUSTER");
   return !(v && v[0] == '0');
@@ -1179,6 +1188,7 @@ static bool dispatch_cluster(int dt, bool fast, ScanParams& p, cudaStream_t s, b
     if (dt == kF64) return false;
     if (p.rows * (int64_t)ctas > 0x7FFFFFFFll) return false;
     p.ctas_per_row = ctas;
+    p.withheld_key_bytes = withheld_key_bytes();
     switch (dt) {
       case kBF16:
         *err = fast ? launch_cluster_t<kBF16, true, MODE>(p, warps, s, pdl)
