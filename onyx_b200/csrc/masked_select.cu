@@ -259,24 +259,26 @@ struct WarpSegment {
     const float mf = __uint_as_float((M & 0x80000000u) ? (M & 0x7FFFFFFFu) : ~M);
     uint32_t key = 0xFFFFFFFFu;
     uint32_t m2 = 0u;
-    if (tord == M) {  // only lanes whose maximum is M can hold it
-      // each vector's masked maximum is recomputed here rather than kept from phase 1:
-      // only the lanes holding the maximum get this far
-      if constexpr (DT == kF32) {
+    if constexpr (DT == kF32) {
+      if (tord == M) {  // only lanes whose maximum is M can hold it
+        // f32 keeps no per-vector maxima: recompute them in the lanes that get here
 #pragma unroll
         for (int k = UNROLL - 1; k >= 0; --k)
           if ((bits[k] & kLaneBits) && V::masked_max(x[k], bits[k]) == mf)
             key = ((uint32_t)k << 5) | lane;
-      } else {
-        const uint32_t h = V::from_f32(mf);
-        m2 = h | (h << 16);
-#pragma unroll
-        for (int k = UNROLL - 1; k >= 0; --k)
-          if ((bits[k] & kLaneBits) && V::eq_mask(vm[k], m2)) key = ((uint32_t)k << 5) | lane;
       }
-      if (key == 0xFFFFFFFFu && tail_bit && ord32(V::scalar(tail_raw)) == M)
-        key = ((uint32_t)UNROLL << 5) | lane;  // the ragged tail follows every full vector
+    } else {
+      // branch-free over the lanes: which kept vector maxima equal M, as a bit per vector
+      const uint32_t h = V::from_f32(mf);
+      m2 = h | (h << 16);
+      uint32_t hit = 0u;
+#pragma unroll
+      for (int k = 0; k < UNROLL; ++k)
+        hit |= ((bits[k] & kLaneBits) && V::eq_mask(vm[k], m2)) ? (1u << k) : 0u;
+      if (tord == M && hit) key = ((uint32_t)(__ffs(hit) - 1) << 5) | lane;
     }
+    if (tord == M && key == 0xFFFFFFFFu && tail_bit && ord32(V::scalar(tail_raw)) == M)
+      key = ((uint32_t)UNROLL << 5) | lane;  // the ragged tail follows every full vector
     const uint32_t win = __reduce_min_sync(kFull, key);
     if (win == 0xFFFFFFFFu) return 0xFFFFFFFFu;
     const int wk = (int)(win >> 5), wl = (int)(win & 31u);
