@@ -284,6 +284,10 @@ def run_ours(args) -> None:
 
     name = args.workload
     spec = WORKLOADS[name]
+    if name == "vocab_parallel" and not distributed:
+        # one rank still selects through the exchange path: a single-member group
+        dist.init_process_group("nccl", store=dist.HashStore(), rank=0, world_size=1,
+                                device_id=dev)
     props = torch.cuda.get_device_properties(dev)
     l2 = int(getattr(props, "L2_cache_size", 126 * 2**20))
 
@@ -295,6 +299,7 @@ def run_ours(args) -> None:
 
     # ---- inputs, one seeded set copied into R rotating device buffers -------------------
     seed_shift = 17 * rank
+    exchange = None  # vocab_parallel over NVLink peer memory (collective set-up)
     if name == "batched":
         w = workloads.batched(seed=workloads.SEEDS[2] + seed_shift)
         host_in = {"x": w["logits_bf16"], "m": w["masks"]}
@@ -312,6 +317,8 @@ def run_ours(args) -> None:
         w = workloads.scaling(seed=workloads.SEEDS[5] + seed_shift, rows=spec["rows"])
         host_in = {"x": w["logits_bf16"], "m": w["masks"]}
     elif name == "vocab_parallel":
+        if args.exchange == "peer":
+            exchange = vocab_parallel.PeerExchange(rows_cap=spec["rows"], device=dev)
         w = workloads.scaling(seed=workloads.SEEDS[5], rows=spec["rows"])
         lo, hi = vocab_parallel.vocab_shard_bounds(spec["vocab"], rank, world)
         host_in = {"x": np.ascontiguousarray(w["logits_bf16"][:, lo:hi]),
@@ -343,7 +350,8 @@ def run_ours(args) -> None:
         if name == "spec_verify":
             return ms.spec_verify(b["x"], b["m"], b["d"])
         if name == "vocab_parallel":
-            return vocab_parallel.vocab_parallel_masked_argmax(b["x"], b["m"], col_offset)
+            return vocab_parallel.vocab_parallel_masked_argmax(b["x"], b["m"], col_offset,
+                                                               exchange=exchange)
         raise AssertionError
 
     launches_per_step = 1 if name != "vocab_parallel" else 2
@@ -462,7 +470,8 @@ def run_ours(args) -> None:
             r = ms.spec_verify(xin, dev_in["m"], dev_in["d"])
             out = (r.accept_len, r.correction)
         else:
-            r = vocab_parallel.vocab_parallel_masked_argmax(xin, dev_in["m"], col_offset)
+            r = vocab_parallel.vocab_parallel_masked_argmax(xin, dev_in["m"], col_offset,
+                                                            exchange=exchange)
             out = (r.token_ids, r.status)
         out_host[0].copy_(out[0], non_blocking=True)
         out_host[1].copy_(out[1], non_blocking=True)
@@ -492,7 +501,9 @@ def run_ours(args) -> None:
         v, threads, sample, _, _ = cpu_measure(name, budget_s=args.cpu_seconds)
         cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
 
-    if distributed:
+    if exchange is not None:
+        exchange.close()
+    if dist.is_initialized():
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
@@ -516,7 +527,9 @@ def run_ours(args) -> None:
             "desc": spec["desc"],
             "rows_per_step_per_gpu": rows_per_step,
             "parallelism": (f"batch-sharded x{world}" if name != "vocab_parallel"
-                            else f"vocab-sharded x{world}"),
+                            else f"vocab-sharded x{world}, keys exchanged by "
+                                 + ("NVLink peer stores" if exchange is not None
+                                    else "NCCL all-gather")),
             "l2_policy": f"{R} rotating input sets ({R * set_bytes / 1e6:.0f} MB > 2 x L2 "
                          f"{l2 / 1e6:.0f} MB)",
             "timing": "CUDA events on the launching stream, CUDA-graph replay of the steps, max over ranks",
@@ -541,6 +554,8 @@ def main() -> None:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="batched")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="vocab_parallel: keys over NVLink peer memory, or an NCCL all-gather")
     ap.add_argument("--preheat-seconds", type=float, default=0.5,
                     help="untimed replays before the warm-up, to bring the SM clock up")
     args = ap.parse_args()

@@ -154,6 +154,36 @@ ONYX_API int onyx_combine_partials(const uint64_t* keys, int64_t n_parts, int64_
                           uint32_t* out_status, void* stream);
 
 /*
+ * Vocabulary-parallel selection with the key exchange over NVLink peer memory instead of a
+ * collective library call: the shard-key kernel writes each row's key straight into every
+ * rank's exchange buffer, and one small kernel raises this rank's flag in every buffer
+ * (system-scope release), waits until every rank's flag in its own buffer reaches `epoch`
+ * (bounded: rows get ONYX_STATUS_WAIT_TIMEOUT if it gives up) and combines.
+ * Replaces the all-gather + onyx_combine_partials pair above with identical results. No
+ * counterpart in the reference (single device only; torch_backend.py:970-1007 is the
+ * selection it distributes).
+ *
+ * Exchange buffers: every rank allocates onyx_exchange_buffer_bytes(world, rows_cap) with
+ * onyx_ipc_alloc, shares the onyx_ipc_handle_bytes()-byte handle with the other ranks (any
+ * host channel), and opens theirs with onyx_ipc_open. `exchange_bases[i]` is rank i's
+ * buffer as mapped in this process (its own at [rank]). Every rank makes the same calls in
+ * the same order with the same strictly increasing epoch (1, 2, ...). world <= 8.
+ */
+ONYX_API size_t onyx_ipc_handle_bytes(void);
+ONYX_API size_t onyx_exchange_buffer_bytes(int world, int64_t rows_cap);
+ONYX_API int onyx_ipc_alloc(size_t bytes, void** dev_ptr, void* handle_out);
+ONYX_API int onyx_ipc_open(const void* handle, void** dev_ptr);
+ONYX_API int onyx_ipc_close(void* dev_ptr);
+ONYX_API int onyx_ipc_free(void* dev_ptr);
+ONYX_API int onyx_vocab_exchange_argmax(const void* logits, int dtype, int64_t rows,
+                                        int64_t shard_vocab, int64_t row_stride,
+                                        const uint32_t* mask, int64_t mask_stride,
+                                        int64_t col_offset, int world, int rank,
+                                        void* const* exchange_bases, int64_t rows_cap,
+                                        uint64_t epoch, int32_t* out_idx, uint32_t* out_status,
+                                        void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Allocation-free masked greedy selection. No counterpart in the reference: it is the
  * onyx_masked_argmax contract for callers that cannot allocate device memory when they
  * call -- a serving process whose GPU memory is reserved up front by its own pool, a

@@ -29,6 +29,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #ifndef ONYX_PDL_EARLY
@@ -70,6 +71,11 @@ struct ScanParams {
   // test hook: key bytes rank 0 of the cluster path expects beyond those sent (0 normally;
   // nonzero makes its bounded wait run out)
   uint32_t withheld_key_bytes;
+  // key mode with a peer exchange: row r's key goes to key_dst[i][r] for every i < n_key_dst
+  // (this rank's slot in every rank's exchange buffer, the peers' over NVLink) instead of
+  // out_key
+  unsigned long long* key_dst[8];
+  int n_key_dst;
 };
 
 constexpr int kMaxPerGroup = 256;
@@ -505,7 +511,11 @@ __device__ void finalize_group(const ScanParams& p, int64_t group, const Partial
       unsigned long long key = 0ull;
       if (r.flags & kFlagAny) key = (r.ord << 32) | (unsigned long long)(0xFFFFFFFFu - r.idx);
       if (r.flags & kFlagWaitTimeout) key = kKeyWaitTimeout;
-      p.out_key[group] = key;
+      if (p.n_key_dst) {
+        for (int i = 0; i < p.n_key_dst; ++i) p.key_dst[i][group] = key;
+      } else {
+        p.out_key[group] = key;
+      }
     }
   } else {
     // speculative verify: members in position order; the first row that differs from
@@ -1067,6 +1077,8 @@ __global__ void combine_keys_kernel(const unsigned long long* keys, int64_t n_pa
   decode_partial(pr, false, &out_idx[r], &out_status[r]);
 }
 
+#include "peer_exchange.cuh"
+
 // ---------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------
@@ -1482,6 +1494,132 @@ int onyx_vocab_partial_argmax(const void* logits, int dtype, int64_t rows, int64
   rc = bind_workspace(p, workspace, workspace_bytes, workspace_bytes_for(rows, rows, pl, 1), rows);
   if (rc) return rc;
   return finish_launch(dispatch<kModeKey>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled()));
+}
+
+size_t onyx_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+size_t onyx_exchange_buffer_bytes(int world, int64_t rows_cap) {
+  if (world < 1 || world > kMaxExchangeRanks || rows_cap < 1) return 0;
+  return kExchangeFlagBytes + (size_t)2 * world * rows_cap * sizeof(unsigned long long);
+}
+
+int onyx_ipc_alloc(size_t bytes, void** dev_ptr, void* handle_out) {
+  if (!bytes || !dev_ptr || !handle_out) return ONYX_ERR_INVALID_ARGUMENT;
+  void* ptr = nullptr;
+  cudaError_t e = cudaMalloc(&ptr, bytes);
+  if (e == cudaSuccess) e = cudaMemset(ptr, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle_out), ptr);
+  if (e != cudaSuccess) {
+    if (ptr) cudaFree(ptr);
+    g_last_cuda_error = (int)e;
+    return ONYX_ERR_CUDA;
+  }
+  *dev_ptr = ptr;
+  return ONYX_OK;
+}
+
+int onyx_ipc_open(const void* handle, void** dev_ptr) {
+  if (!handle || !dev_ptr) return ONYX_ERR_INVALID_ARGUMENT;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    g_last_cuda_error = (int)e;
+    return ONYX_ERR_CUDA;
+  }
+  return ONYX_OK;
+}
+
+int onyx_ipc_close(void* dev_ptr) {
+  if (!dev_ptr) return ONYX_ERR_INVALID_ARGUMENT;
+  const cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  if (e != cudaSuccess) {
+    g_last_cuda_error = (int)e;
+    return ONYX_ERR_CUDA;
+  }
+  return ONYX_OK;
+}
+
+int onyx_ipc_free(void* dev_ptr) {
+  if (!dev_ptr) return ONYX_ERR_INVALID_ARGUMENT;
+  const cudaError_t e = cudaFree(dev_ptr);
+  if (e != cudaSuccess) {
+    g_last_cuda_error = (int)e;
+    return ONYX_ERR_CUDA;
+  }
+  return ONYX_OK;
+}
+
+int onyx_vocab_exchange_argmax(const void* logits, int dtype, int64_t rows, int64_t shard_vocab,
+                               int64_t row_stride, const uint32_t* mask, int64_t mask_stride,
+                               int64_t col_offset, int world, int rank,
+                               void* const* exchange_bases, int64_t rows_cap, uint64_t epoch,
+                               int32_t* out_idx, uint32_t* out_status, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (dtype == kF64) return ONYX_ERR_UNSUPPORTED_DTYPE;
+  int rc = common_checks(logits, dtype, rows, shard_vocab, row_stride);
+  if (rc) return rc;
+  if (world < 1 || world > kMaxExchangeRanks || rank < 0 || rank >= world || !exchange_bases ||
+      epoch == 0 || rows > rows_cap || !out_idx || !out_status)
+    return ONYX_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < world; ++i)
+    if (!exchange_bases[i] || ((uintptr_t)exchange_bases[i] & 255u)) return ONYX_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return ONYX_OK;
+  if (!mask || col_offset < 0 || (col_offset & 31) || col_offset + shard_vocab > 0x7FFFFFFFll - 1)
+    return ONYX_ERR_INVALID_ARGUMENT;
+  if (mask_stride < (shard_vocab + 31) / 32 && rows > 1) return ONYX_ERR_INVALID_ARGUMENT;
+  const int es = dtype_bytes(dtype);
+  const bool aligned = aligned16(logits) && ((row_stride * es) % 16 == 0 || rows == 1);
+  const Plan pl = make_plan(dtype, shard_vocab, aligned);
+  const int parity = (int)(epoch & 1ull);
+  ScanParams p = {};
+  p.logits = logits;
+  p.group_stride = row_stride;
+  p.vocab = shard_vocab;
+  p.mask = mask;
+  p.mask_group_stride = mask_stride;
+  p.idx_offset = col_offset;
+  p.rows = rows;
+  p.per_group = 1;
+  p.segs = pl.segs;
+  p.ctas_per_row = pl.ctas_per_row;
+  p.seg_elems = pl.seg_elems;
+  p.n_key_dst = world;
+  ExchangeParams x = {};
+  for (int i = 0; i < world; ++i) {
+    char* base = static_cast<char*>(exchange_bases[i]);
+    p.key_dst[i] = reinterpret_cast<unsigned long long*>(base + kExchangeFlagBytes) +
+                   ((int64_t)parity * world + rank) * rows_cap;
+    x.flag_dst[i] = reinterpret_cast<unsigned long long*>(base) + rank;
+  }
+  char* own = static_cast<char*>(exchange_bases[rank]);
+  x.own_flags = reinterpret_cast<unsigned long long*>(own);
+  x.slots = reinterpret_cast<const unsigned long long*>(own + kExchangeFlagBytes) +
+            (int64_t)parity * world * rows_cap;
+  x.world = world;
+  x.rows = rows;
+  x.rows_cap = rows_cap;
+  x.epoch = epoch;
+  x.out_idx = out_idx;
+  x.out_status = out_status;
+  const bool pdl = pdl_enabled();
+  cudaError_t err = cudaSuccess;
+  if (!dispatch_cluster<kModeKey>(dtype, pl.fast, p, (cudaStream_t)stream, pdl, &err)) {
+    rc = bind_workspace(p, workspace, workspace_bytes, workspace_bytes_for(rows, rows, pl, 1), rows);
+    if (rc) return rc;
+    err = dispatch<kModeKey>(dtype, pl.fast, p, (cudaStream_t)stream, pdl);
+  }
+  if (err != cudaSuccess) return finish_launch(err);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, 1, 1);
+  cfg.blockDim = dim3(1024, 1, 1);
+  cfg.stream = (cudaStream_t)stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return finish_launch(cudaLaunchKernelEx(&cfg, exchange_combine_kernel, x));
 }
 
 static Plan make_apply_plan(int dt, int64_t vocab, bool aligned) {

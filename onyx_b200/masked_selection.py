@@ -36,6 +36,7 @@ __all__ = [
     "mask_apply",
     "vocab_partial_keys",
     "combine_partial_keys",
+    "vocab_exchange_argmax",
     "mask_words",
     "dtype_code",
     "STATUS_EMPTY_MASK",
@@ -363,6 +364,46 @@ def vocab_partial_keys(
             ),
         )
     return keys
+
+
+def vocab_exchange_argmax(
+    logits_shard: torch.Tensor, mask_shard: torch.Tensor, col_offset: int, *, world: int,
+    rank: int, exchange_bases, rows_cap: int, epoch: int,
+) -> MaskedArgmaxResult:
+    """Full-vocabulary selections from this rank's shard, the keys exchanged through the
+    ranks' NVLink-mapped exchange buffers (``exchange_bases``: a ctypes array of ``world``
+    device pointers, this rank's own at ``rank``). Every rank calls it with the same epoch.
+    Use :class:`onyx_b200.vocab_parallel.PeerExchange` rather than calling this directly."""
+    x = _logits_2d(logits_shard, "logits_shard")
+    rows, vocab = x.shape
+    if x.dtype == torch.float64:
+        raise TypeError("vocabulary-sharded selection supports float32/float16/bfloat16")
+    if col_offset < 0 or col_offset % 32:
+        raise ValueError("col_offset must be a non-negative multiple of 32")
+    if rows > rows_cap:
+        raise ValueError(f"{rows} rows exceed the exchange buffers' capacity of {rows_cap}")
+    m = _mask_2d(mask_shard, rows, vocab, "mask_shard")
+    device = _same_device(x, m)
+    idx = torch.empty(rows, dtype=torch.int32, device=device)
+    status = torch.empty(rows, dtype=torch.int32, device=device)
+    if rows == 0:
+        return MaskedArgmaxResult(idx, status)
+    lib = _lib.load()
+    code = dtype_code(x.dtype)
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device)
+        need = lib.onyx_vocab_partial_workspace_size(rows, vocab, code)
+        ws = _WORKSPACES.get(device, stream, need)
+        _lib.check(
+            "onyx_vocab_exchange_argmax",
+            lib.onyx_vocab_exchange_argmax(
+                x.data_ptr(), code, rows, vocab, x.stride(0) if rows > 1 else vocab,
+                m.data_ptr(), m.stride(0), int(col_offset), int(world), int(rank),
+                exchange_bases, int(rows_cap), int(epoch), idx.data_ptr(), status.data_ptr(),
+                _ptr(ws), 0 if ws is None else ws.numel(), stream.cuda_stream,
+            ),
+        )
+    return MaskedArgmaxResult(idx, status)
 
 
 def combine_partial_keys(keys: torch.Tensor) -> MaskedArgmaxResult:

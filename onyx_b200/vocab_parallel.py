@@ -17,17 +17,23 @@ selection over one process per GPU:
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from . import masked_selection as _ms
 
 __all__ = [
     "batch_shard_bounds",
     "vocab_shard_bounds",
+    "PeerExchange",
     "vocab_parallel_masked_argmax",
     "combine_keys_host",
 ]
+
+MAX_EXCHANGE_RANKS = 8
 
 
 def batch_shard_bounds(rows: int, rank: int, world_size: int) -> tuple[int, int]:
@@ -49,16 +55,95 @@ def vocab_shard_bounds(vocab: int, rank: int, world_size: int) -> tuple[int, int
     return min(wlo * 32, vocab), min(whi * 32, vocab)
 
 
+class PeerExchange:
+    """Exchange buffers of one process group for vocabulary-sharded selection over NVLink
+    peer memory: each rank's buffer is mapped into every other rank (CUDA IPC), the shard
+    kernel writes its row keys straight into all of them, and a small kernel swaps flags
+    and combines -- one fused step instead of an all-gather plus a combine.
+
+    Collective: every rank of ``group`` constructs it with the same ``rows_cap`` (the most
+    rows one call may select), makes the same calls in the same order, and closes it.
+    """
+
+    def __init__(self, rows_cap: int, group: dist.ProcessGroup | None = None,
+                 device: torch.device | int | None = None) -> None:
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if not 1 <= self.world <= MAX_EXCHANGE_RANKS:
+            raise ValueError(f"peer exchange supports 1..{MAX_EXCHANGE_RANKS} ranks")
+        if rows_cap < 1:
+            raise ValueError("rows_cap must be positive")
+        self.rows_cap = int(rows_cap)
+        if device is None:
+            device = torch.cuda.current_device()
+        self.device = device if isinstance(device, torch.device) else torch.device("cuda", device)
+        self.epoch = 0
+        self._lib = lib = _lib.load()
+        nbytes = lib.onyx_exchange_buffer_bytes(self.world, self.rows_cap)
+        handle = ctypes.create_string_buffer(lib.onyx_ipc_handle_bytes())
+        own = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check("onyx_ipc_alloc", lib.onyx_ipc_alloc(nbytes, ctypes.byref(own), handle))
+        handles: list[bytes | None] = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self._opened: list[int] = []
+        bases = []
+        with torch.cuda.device(self.device):
+            for i, h in enumerate(handles):
+                if i == self.rank:
+                    bases.append(own.value)
+                    continue
+                ptr = ctypes.c_void_p()
+                _lib.check("onyx_ipc_open", lib.onyx_ipc_open(h, ctypes.byref(ptr)))
+                self._opened.append(ptr.value)
+                bases.append(ptr.value)
+        self._own = own.value
+        self.bases = (ctypes.c_void_p * self.world)(*bases)
+        dist.barrier(group)  # every mapping exists before any rank stores into it
+
+    def select(self, logits_shard: torch.Tensor, mask_shard: torch.Tensor,
+               col_offset: int) -> _ms.MaskedArgmaxResult:
+        """This call's full-vocabulary selections (same call on every rank)."""
+        if self._own is None:
+            raise RuntimeError("the peer exchange is closed")
+        if logits_shard.shape[-1] == 0:
+            raise ValueError("every rank of a peer exchange must hold at least one column")
+        self.epoch += 1
+        return _ms.vocab_exchange_argmax(
+            logits_shard, mask_shard, col_offset, world=self.world, rank=self.rank,
+            exchange_bases=self.bases, rows_cap=self.rows_cap, epoch=self.epoch)
+
+    def close(self) -> None:
+        """Collective: unmaps the peers' buffers and frees this rank's."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)  # no rank still stores into another's buffer
+        with torch.cuda.device(self.device):
+            for ptr in self._opened:
+                _lib.check("onyx_ipc_close", self._lib.onyx_ipc_close(ptr))
+            dist.barrier(self.group)
+            _lib.check("onyx_ipc_free", self._lib.onyx_ipc_free(self._own))
+        self._own = None
+        self._opened = []
+
+
 def vocab_parallel_masked_argmax(
     logits_shard: torch.Tensor,
     mask_shard: torch.Tensor,
     col_offset: int,
     group: dist.ProcessGroup | None = None,
+    exchange: PeerExchange | None = None,
 ) -> _ms.MaskedArgmaxResult:
     """Masked greedy selection over a vocabulary split across the ranks of ``group``.
 
-    Every rank passes its own shard and receives the full-vocabulary selections.
+    Every rank passes its own shard and receives the full-vocabulary selections. With a
+    :class:`PeerExchange` the keys travel through NVLink peer memory inside the selection
+    step; without one they travel by ``all_gather_into_tensor`` (any backend).
     """
+    if exchange is not None:
+        return exchange.select(logits_shard, mask_shard, col_offset)
     world = dist.get_world_size(group)
     if logits_shard.shape[-1] == 0:
         # a rank past the end of a small vocabulary holds no columns: key 0 = no token

@@ -100,3 +100,96 @@ def test_nccl_vocab_parallel_two_ranks(tmp_path, cuda_lib):
     idx_ref, st_ref = oracle.masked_argmax(w["logits_bf16"], w["masks"], dtype="bf16")
     np.testing.assert_array_equal(got[0], idx_ref)
     np.testing.assert_array_equal(got[1].astype(np.uint32), st_ref)
+
+
+def test_peer_exchange_single_rank_matches_oracle(cuda_lib):
+    """world = 1: the key kernel stores into the rank's own exchange buffer, the exchange
+    kernel raises and reads its own flag; consecutive epochs alternate the two parities."""
+    import ctypes
+    from onyx_b200 import _lib
+    lib = cuda_lib
+    rows, rows_cap = 64, 96
+    nbytes = lib.onyx_exchange_buffer_bytes(1, rows_cap)
+    handle = ctypes.create_string_buffer(lib.onyx_ipc_handle_bytes())
+    own = ctypes.c_void_p()
+    assert lib.onyx_ipc_alloc(nbytes, ctypes.byref(own), handle) == _lib.OK
+    bases = (ctypes.c_void_p * 1)(own.value)
+    try:
+        for epoch, seed in ((1, 3), (2, 4), (3, 5)):
+            w = workloads.scaling(seed=seed, rows=rows, vocab=32000)
+            x, m = w["logits_bf16"], w["masks"]
+            idx_ref, st_ref = oracle.masked_argmax(x, m, dtype="bf16")
+            res = ms.vocab_exchange_argmax(to_device(x, "bf16"), masks_to_device(m), 0, world=1,
+                                           rank=0, exchange_bases=bases, rows_cap=rows_cap,
+                                           epoch=epoch)
+            np.testing.assert_array_equal(host(res.token_ids), idx_ref)
+            np.testing.assert_array_equal(host(res.status).astype(np.uint32), st_ref)
+    finally:
+        torch.cuda.synchronize()
+        assert lib.onyx_ipc_free(own.value) == _lib.OK
+
+
+def test_peer_exchange_rejects_bad_arguments(cuda_lib):
+    import ctypes
+    from onyx_b200 import _lib
+    lib = cuda_lib
+    bases = (ctypes.c_void_p * 1)(None)
+    x = torch.zeros((2, 64), dtype=torch.bfloat16, device="cuda:0")
+    m = torch.zeros((2, 2), dtype=torch.int32, device="cuda:0")
+    out = torch.empty(2, dtype=torch.int32, device="cuda:0")
+    args = [x.data_ptr(), _lib.DTYPE_BF16, 2, 64, 64, m.data_ptr(), 2, 0]
+    # a null buffer, epoch 0, rank outside the world, more rows than the buffers hold
+    for world, rank, cap, epoch in ((1, 0, 4, 1), (1, 0, 4, 0), (1, 1, 4, 1), (1, 0, 1, 1)):
+        rc = lib.onyx_vocab_exchange_argmax(*args, world, rank, bases, cap, epoch, out.data_ptr(),
+                                            out.data_ptr(), None, 0, None)
+        assert rc == _lib.ERR_INVALID_ARGUMENT
+    assert lib.onyx_exchange_buffer_bytes(9, 4) == 0
+
+
+_PEER_WORKER = r"""
+import os, sys, numpy as np, torch, torch.distributed as dist
+sys.path.insert(0, os.environ["ONYX_ROOT"])
+from onyx_b200 import vocab_parallel, workloads
+rank = int(os.environ["RANK"]); world = int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
+ex = vocab_parallel.PeerExchange(rows_cap=128)
+outs = []
+for seed in (11, 12, 13):  # three epochs: both parities, then the first again
+    w = workloads.scaling(seed=seed, rows=128, vocab=32000 * world)
+    x, m = w["logits_bf16"], w["masks"]
+    lo, hi = vocab_parallel.vocab_shard_bounds(x.shape[1], rank, world)
+    xt = torch.from_numpy(np.ascontiguousarray(x[:, lo:hi]).view(np.int16)).cuda().view(torch.bfloat16)
+    mt = torch.from_numpy(np.ascontiguousarray(m[:, lo // 32:(hi + 31) // 32]).view(np.int32)).cuda()
+    res = vocab_parallel.vocab_parallel_masked_argmax(xt, mt, lo, exchange=ex)
+    ref = vocab_parallel.vocab_parallel_masked_argmax(xt, mt, lo)  # NCCL all-gather
+    assert torch.equal(res.token_ids, ref.token_ids) and torch.equal(res.status, ref.status)
+    outs.append(torch.stack((res.token_ids, res.status)).cpu().numpy())
+ex.close()
+if rank == 0:
+    np.save(os.environ["ONYX_OUT"], np.stack(outs))
+dist.barrier()
+dist.destroy_process_group()
+"""
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_exchange_two_ranks(tmp_path, cuda_lib):
+    world = 2
+    script = tmp_path / "peer_worker.py"
+    script.write_text(_PEER_WORKER)
+    out = tmp_path / "peer_out.npy"
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    env = dict(os.environ, ONYX_ROOT=str(Path(__file__).resolve().parents[1]), ONYX_OUT=str(out),
+               NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr", "127.0.0.1", "--master-port", str(port), str(script)]
+    subprocess.run(["timeout", "-k", "30", "300", *cmd], check=True, env=env)
+    got = np.load(out)
+    for k, seed in enumerate((11, 12, 13)):
+        w = workloads.scaling(seed=seed, rows=128, vocab=32000 * world)
+        idx_ref, st_ref = oracle.masked_argmax(w["logits_bf16"], w["masks"], dtype="bf16")
+        np.testing.assert_array_equal(got[k, 0], idx_ref)
+        np.testing.assert_array_equal(got[k, 1].astype(np.uint32), st_ref)
