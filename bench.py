@@ -362,7 +362,9 @@ def run_ours(args) -> None:
         for k in range(R):
             step(k)  # warm the workspace for this stream and load the library
     stream.synchronize()
-    use_graphs = name != "vocab_parallel"
+    # the peer exchange counts its calls on the device, so its steps replay from graphs too;
+    # the NCCL path is replayed eagerly
+    use_graphs = name != "vocab_parallel" or exchange is not None
     chunk = min(args.steps, 1024)
 
     def make_graph(n: int):

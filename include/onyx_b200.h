@@ -157,8 +157,8 @@ ONYX_API int onyx_combine_partials(const uint64_t* keys, int64_t n_parts, int64_
  * Vocabulary-parallel selection with the key exchange over NVLink peer memory instead of a
  * collective library call: the shard-key kernel writes each row's key straight into every
  * rank's exchange buffer, and one small kernel raises this rank's flag in every buffer
- * (system-scope release), waits until every rank's flag in its own buffer reaches `epoch`
- * (bounded: rows get ONYX_STATUS_WAIT_TIMEOUT if it gives up) and combines.
+ * (system-scope release), waits until every rank's flag in its own buffer reaches this
+ * call's number (bounded: rows get ONYX_STATUS_WAIT_TIMEOUT if it gives up) and combines.
  * Replaces the all-gather + onyx_combine_partials pair above with identical results. No
  * counterpart in the reference (single device only; torch_backend.py:970-1007 is the
  * selection it distributes).
@@ -167,7 +167,8 @@ ONYX_API int onyx_combine_partials(const uint64_t* keys, int64_t n_parts, int64_
  * onyx_ipc_alloc, shares the onyx_ipc_handle_bytes()-byte handle with the other ranks (any
  * host channel), and opens theirs with onyx_ipc_open. `exchange_bases[i]` is rank i's
  * buffer as mapped in this process (its own at [rank]). Every rank makes the same calls in
- * the same order with the same strictly increasing epoch (1, 2, ...). world <= 8.
+ * the same order; each rank's buffer counts its finished calls on the device, so the calls
+ * may be captured in a CUDA graph and replayed. world <= 8.
  */
 ONYX_API size_t onyx_ipc_handle_bytes(void);
 ONYX_API size_t onyx_exchange_buffer_bytes(int world, int64_t rows_cap);
@@ -180,7 +181,7 @@ ONYX_API int onyx_vocab_exchange_argmax(const void* logits, int dtype, int64_t r
                                         const uint32_t* mask, int64_t mask_stride,
                                         int64_t col_offset, int world, int rank,
                                         void* const* exchange_bases, int64_t rows_cap,
-                                        uint64_t epoch, int32_t* out_idx, uint32_t* out_status,
+                                        int32_t* out_idx, uint32_t* out_status,
                                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*

@@ -65,7 +65,7 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "onyx_ipc_free": (_i32, [_vp]),
     "onyx_vocab_exchange_argmax": (
         _i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _i64, _i32, _i32, ctypes.POINTER(_vp),
-               _i64, ctypes.c_uint64, _vp, _vp, _vp, _sz, _vp]),
+               _i64, _vp, _vp, _vp, _sz, _vp]),
 }
 
 

@@ -71,11 +71,14 @@ struct ScanParams {
   // test hook: key bytes rank 0 of the cluster path expects beyond those sent (0 normally;
   // nonzero makes its bounded wait run out)
   uint32_t withheld_key_bytes;
-  // key mode with a peer exchange: row r's key goes to key_dst[i][r] for every i < n_key_dst
-  // (this rank's slot in every rank's exchange buffer, the peers' over NVLink) instead of
-  // out_key
+  // key mode with a peer exchange: row r's key goes to key_dst[i][parity * key_parity_stride
+  // + r] for every i < n_key_dst (this rank's slot in every rank's exchange buffer, the
+  // peers' over NVLink) instead of out_key; the parity is that of this call's epoch, one
+  // above the count kept in this rank's buffer at key_epoch
   unsigned long long* key_dst[8];
   int n_key_dst;
+  int64_t key_parity_stride;
+  const unsigned long long* key_epoch;
 };
 
 constexpr int kMaxPerGroup = 256;
@@ -512,7 +515,8 @@ __device__ void finalize_group(const ScanParams& p, int64_t group, const Partial
       if (r.flags & kFlagAny) key = (r.ord << 32) | (unsigned long long)(0xFFFFFFFFu - r.idx);
       if (r.flags & kFlagWaitTimeout) key = kKeyWaitTimeout;
       if (p.n_key_dst) {
-        for (int i = 0; i < p.n_key_dst; ++i) p.key_dst[i][group] = key;
+        const int64_t slot = ((__ldcg(p.key_epoch) + 1ull) & 1ull ? p.key_parity_stride : 0) + group;
+        for (int i = 0; i < p.n_key_dst; ++i) p.key_dst[i][slot] = key;
       } else {
         p.out_key[group] = key;
       }
@@ -1553,14 +1557,14 @@ int onyx_ipc_free(void* dev_ptr) {
 int onyx_vocab_exchange_argmax(const void* logits, int dtype, int64_t rows, int64_t shard_vocab,
                                int64_t row_stride, const uint32_t* mask, int64_t mask_stride,
                                int64_t col_offset, int world, int rank,
-                               void* const* exchange_bases, int64_t rows_cap, uint64_t epoch,
+                               void* const* exchange_bases, int64_t rows_cap,
                                int32_t* out_idx, uint32_t* out_status, void* workspace,
                                size_t workspace_bytes, void* stream) {
   if (dtype == kF64) return ONYX_ERR_UNSUPPORTED_DTYPE;
   int rc = common_checks(logits, dtype, rows, shard_vocab, row_stride);
   if (rc) return rc;
   if (world < 1 || world > kMaxExchangeRanks || rank < 0 || rank >= world || !exchange_bases ||
-      epoch == 0 || rows > rows_cap || !out_idx || !out_status)
+      rows > rows_cap || !out_idx || !out_status)
     return ONYX_ERR_INVALID_ARGUMENT;
   for (int i = 0; i < world; ++i)
     if (!exchange_bases[i] || ((uintptr_t)exchange_bases[i] & 255u)) return ONYX_ERR_INVALID_ARGUMENT;
@@ -1571,7 +1575,6 @@ int onyx_vocab_exchange_argmax(const void* logits, int dtype, int64_t rows, int6
   const int es = dtype_bytes(dtype);
   const bool aligned = aligned16(logits) && ((row_stride * es) % 16 == 0 || rows == 1);
   const Plan pl = make_plan(dtype, shard_vocab, aligned);
-  const int parity = (int)(epoch & 1ull);
   ScanParams p = {};
   p.logits = logits;
   p.group_stride = row_stride;
@@ -1584,22 +1587,25 @@ int onyx_vocab_exchange_argmax(const void* logits, int dtype, int64_t rows, int6
   p.segs = pl.segs;
   p.ctas_per_row = pl.ctas_per_row;
   p.seg_elems = pl.seg_elems;
+  char* own = static_cast<char*>(exchange_bases[rank]);
+  unsigned long long* own_epoch = reinterpret_cast<unsigned long long*>(own + kExchangeEpochOffset);
   p.n_key_dst = world;
+  p.key_parity_stride = (int64_t)world * rows_cap;
+  p.key_epoch = own_epoch;
   ExchangeParams x = {};
   for (int i = 0; i < world; ++i) {
     char* base = static_cast<char*>(exchange_bases[i]);
     p.key_dst[i] = reinterpret_cast<unsigned long long*>(base + kExchangeFlagBytes) +
-                   ((int64_t)parity * world + rank) * rows_cap;
+                   (int64_t)rank * rows_cap;
     x.flag_dst[i] = reinterpret_cast<unsigned long long*>(base) + rank;
   }
-  char* own = static_cast<char*>(exchange_bases[rank]);
   x.own_flags = reinterpret_cast<unsigned long long*>(own);
-  x.slots = reinterpret_cast<const unsigned long long*>(own + kExchangeFlagBytes) +
-            (int64_t)parity * world * rows_cap;
+  x.own_epoch = own_epoch;
+  x.slots = reinterpret_cast<const unsigned long long*>(own + kExchangeFlagBytes);
+  x.parity_stride = (int64_t)world * rows_cap;
   x.world = world;
   x.rows = rows;
   x.rows_cap = rows_cap;
-  x.epoch = epoch;
   x.out_idx = out_idx;
   x.out_status = out_status;
   const bool pdl = pdl_enabled();

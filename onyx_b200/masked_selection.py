@@ -368,12 +368,13 @@ def vocab_partial_keys(
 
 def vocab_exchange_argmax(
     logits_shard: torch.Tensor, mask_shard: torch.Tensor, col_offset: int, *, world: int,
-    rank: int, exchange_bases, rows_cap: int, epoch: int,
+    rank: int, exchange_bases, rows_cap: int,
 ) -> MaskedArgmaxResult:
     """Full-vocabulary selections from this rank's shard, the keys exchanged through the
     ranks' NVLink-mapped exchange buffers (``exchange_bases``: a ctypes array of ``world``
-    device pointers, this rank's own at ``rank``). Every rank calls it with the same epoch.
-    Use :class:`onyx_b200.vocab_parallel.PeerExchange` rather than calling this directly."""
+    device pointers, this rank's own at ``rank``). Every rank makes the same calls in the
+    same order. Use :class:`onyx_b200.vocab_parallel.PeerExchange` rather than calling
+    this directly."""
     x = _logits_2d(logits_shard, "logits_shard")
     rows, vocab = x.shape
     if x.dtype == torch.float64:
@@ -399,7 +400,7 @@ def vocab_exchange_argmax(
             lib.onyx_vocab_exchange_argmax(
                 x.data_ptr(), code, rows, vocab, x.stride(0) if rows > 1 else vocab,
                 m.data_ptr(), m.stride(0), int(col_offset), int(world), int(rank),
-                exchange_bases, int(rows_cap), int(epoch), idx.data_ptr(), status.data_ptr(),
+                exchange_bases, int(rows_cap), idx.data_ptr(), status.data_ptr(),
                 _ptr(ws), 0 if ws is None else ws.numel(), stream.cuda_stream,
             ),
         )

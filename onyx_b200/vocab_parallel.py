@@ -62,7 +62,8 @@ class PeerExchange:
     and combines -- one fused step instead of an all-gather plus a combine.
 
     Collective: every rank of ``group`` constructs it with the same ``rows_cap`` (the most
-    rows one call may select), makes the same calls in the same order, and closes it.
+    rows one call may select), makes the same calls in the same order, and closes it. The
+    call count lives on the device, so calls may be captured in a CUDA graph.
     """
 
     def __init__(self, rows_cap: int, group: dist.ProcessGroup | None = None,
@@ -78,7 +79,6 @@ class PeerExchange:
         if device is None:
             device = torch.cuda.current_device()
         self.device = device if isinstance(device, torch.device) else torch.device("cuda", device)
-        self.epoch = 0
         self._lib = lib = _lib.load()
         nbytes = lib.onyx_exchange_buffer_bytes(self.world, self.rows_cap)
         handle = ctypes.create_string_buffer(lib.onyx_ipc_handle_bytes())
@@ -109,10 +109,9 @@ class PeerExchange:
             raise RuntimeError("the peer exchange is closed")
         if logits_shard.shape[-1] == 0:
             raise ValueError("every rank of a peer exchange must hold at least one column")
-        self.epoch += 1
         return _ms.vocab_exchange_argmax(
             logits_shard, mask_shard, col_offset, world=self.world, rank=self.rank,
-            exchange_bases=self.bases, rows_cap=self.rows_cap, epoch=self.epoch)
+            exchange_bases=self.bases, rows_cap=self.rows_cap)
 
     def close(self) -> None:
         """Collective: unmaps the peers' buffers and frees this rank's."""

@@ -104,7 +104,7 @@ def test_nccl_vocab_parallel_two_ranks(tmp_path, cuda_lib):
 
 def test_peer_exchange_single_rank_matches_oracle(cuda_lib):
     """world = 1: the key kernel stores into the rank's own exchange buffer, the exchange
-    kernel raises and reads its own flag; consecutive epochs alternate the two parities."""
+    kernel raises and reads its own flag; consecutive calls alternate the two parities."""
     import ctypes
     from onyx_b200 import _lib
     lib = cuda_lib
@@ -115,15 +115,33 @@ def test_peer_exchange_single_rank_matches_oracle(cuda_lib):
     assert lib.onyx_ipc_alloc(nbytes, ctypes.byref(own), handle) == _lib.OK
     bases = (ctypes.c_void_p * 1)(own.value)
     try:
-        for epoch, seed in ((1, 3), (2, 4), (3, 5)):
+        for seed in (3, 4, 5):  # three calls: both parities, then the first again
             w = workloads.scaling(seed=seed, rows=rows, vocab=32000)
             x, m = w["logits_bf16"], w["masks"]
             idx_ref, st_ref = oracle.masked_argmax(x, m, dtype="bf16")
             res = ms.vocab_exchange_argmax(to_device(x, "bf16"), masks_to_device(m), 0, world=1,
-                                           rank=0, exchange_bases=bases, rows_cap=rows_cap,
-                                           epoch=epoch)
+                                           rank=0, exchange_bases=bases, rows_cap=rows_cap)
             np.testing.assert_array_equal(host(res.token_ids), idx_ref)
             np.testing.assert_array_equal(host(res.status).astype(np.uint32), st_ref)
+        # captured in a CUDA graph: the device-side call count keeps the parities right
+        w = workloads.scaling(seed=6, rows=rows, vocab=32000)
+        idx_ref, st_ref = oracle.masked_argmax(w["logits_bf16"], w["masks"], dtype="bf16")
+        xt, mt = to_device(w["logits_bf16"], "bf16"), masks_to_device(w["masks"])
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            ms.vocab_exchange_argmax(xt, mt, 0, world=1, rank=0, exchange_bases=bases,
+                                     rows_cap=rows_cap)  # workspace and library warm-up
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            outs = [ms.vocab_exchange_argmax(xt, mt, 0, world=1, rank=0, exchange_bases=bases,
+                                             rows_cap=rows_cap) for _ in range(3)]
+        for _ in range(2):
+            g.replay()
+            torch.cuda.synchronize()
+            for res in outs:
+                np.testing.assert_array_equal(host(res.token_ids), idx_ref)
+                np.testing.assert_array_equal(host(res.status).astype(np.uint32), st_ref)
     finally:
         torch.cuda.synchronize()
         assert lib.onyx_ipc_free(own.value) == _lib.OK
@@ -138,9 +156,9 @@ def test_peer_exchange_rejects_bad_arguments(cuda_lib):
     m = torch.zeros((2, 2), dtype=torch.int32, device="cuda:0")
     out = torch.empty(2, dtype=torch.int32, device="cuda:0")
     args = [x.data_ptr(), _lib.DTYPE_BF16, 2, 64, 64, m.data_ptr(), 2, 0]
-    # a null buffer, epoch 0, rank outside the world, more rows than the buffers hold
-    for world, rank, cap, epoch in ((1, 0, 4, 1), (1, 0, 4, 0), (1, 1, 4, 1), (1, 0, 1, 1)):
-        rc = lib.onyx_vocab_exchange_argmax(*args, world, rank, bases, cap, epoch, out.data_ptr(),
+    # a null buffer, rank outside the world, more rows than the buffers hold, world > 8
+    for world, rank, cap in ((1, 0, 4), (1, 1, 4), (1, 0, 1), (9, 0, 4)):
+        rc = lib.onyx_vocab_exchange_argmax(*args, world, rank, bases, cap, out.data_ptr(),
                                             out.data_ptr(), None, 0, None)
         assert rc == _lib.ERR_INVALID_ARGUMENT
     assert lib.onyx_exchange_buffer_bytes(9, 4) == 0
@@ -155,7 +173,7 @@ torch.cuda.set_device(rank)
 dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
 ex = vocab_parallel.PeerExchange(rows_cap=128)
 outs = []
-for seed in (11, 12, 13):  # three epochs: both parities, then the first again
+for seed in (11, 12, 13):  # three calls: both parities, then the first again
     w = workloads.scaling(seed=seed, rows=128, vocab=32000 * world)
     x, m = w["logits_bf16"], w["masks"]
     lo, hi = vocab_parallel.vocab_shard_bounds(x.shape[1], rank, world)
