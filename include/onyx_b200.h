@@ -154,6 +154,25 @@ ONYX_API int onyx_combine_partials(const uint64_t* keys, int64_t n_parts, int64_
                           uint32_t* out_status, void* stream);
 
 /*
+ * Valid-token bitmasks of DFA states (the mask producer): row r of `out` (out_stride >=
+ * ceil(vocab/32) words) is the packed mask of states[r] -- bit t set iff token t is
+ * non-empty and walking its bytes through `trans` ([n_states][256] next-state ids) from
+ * states[r] does not end in `dead`. Restates get_valid_token_ids,
+ * onyx_cuda/rust/src/regex_runtime.rs:129-145 (transition fold :197-201), for every row in
+ * one launch; building it for every reachable state gives the table that
+ * onyx_gather_masked_argmax reads. Tokens are CSR: tok_bytes[n_bytes], tok_offsets[vocab+1].
+ * `dead_absorbing` nonzero promises every transition from `dead` returns to it (true of
+ * regex-automata's dense DFAs) and lets walks stop there. Out-of-range transitions count as
+ * dead, out-of-range state ids give empty rows, and offsets outside the byte array give empty
+ * tokens, so malformed input is never read out of bounds.
+ */
+ONYX_API int onyx_dfa_state_masks(const int32_t* trans, int32_t n_states, int32_t dead,
+                                  int dead_absorbing, const int32_t* states, int64_t rows,
+                                  const uint8_t* tok_bytes, int64_t n_bytes,
+                                  const int64_t* tok_offsets, int64_t vocab, uint32_t* out,
+                                  int64_t out_stride, void* stream);
+
+/*
  * Vocabulary-parallel selection with the key exchange over NVLink peer memory instead of a
  * collective library call: the shard-key kernel writes each row's key straight into every
  * rank's exchange buffer, and one small kernel raises this rank's flag in every buffer

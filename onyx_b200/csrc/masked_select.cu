@@ -1082,6 +1082,7 @@ __global__ void combine_keys_kernel(const unsigned long long* keys, int64_t n_pa
 }
 
 #include "peer_exchange.cuh"
+#include "dfa_masks.cuh"
 
 // ---------------------------------------------------------------------------------------
 // host side
@@ -1498,6 +1499,49 @@ int onyx_vocab_partial_argmax(const void* logits, int dtype, int64_t rows, int64
   rc = bind_workspace(p, workspace, workspace_bytes, workspace_bytes_for(rows, rows, pl, 1), rows);
   if (rc) return rc;
   return finish_launch(dispatch<kModeKey>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled()));
+}
+
+int onyx_dfa_state_masks(const int32_t* trans, int32_t n_states, int32_t dead,
+                         int dead_absorbing, const int32_t* states, int64_t rows,
+                         const uint8_t* tok_bytes, int64_t n_bytes, const int64_t* tok_offsets,
+                         int64_t vocab, uint32_t* out, int64_t out_stride, void* stream) {
+  if (!trans || n_states < 1 || dead < 0 || dead >= n_states || rows < 0 || vocab < 1 ||
+      vocab > 0x7FFFFFFFll - 1 || !tok_offsets || n_bytes < 0 || (n_bytes > 0 && !tok_bytes) ||
+      out_stride < (vocab + 31) / 32)
+    return ONYX_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return ONYX_OK;
+  if (!states || !out) return ONYX_ERR_INVALID_ARGUMENT;
+  const int64_t words = (vocab + 31) / 32;
+  constexpr int64_t kMaxRowsPerLaunch = (int64_t)65535 * kDfaRowsPerWarp;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  for (int64_t r0 = 0; r0 < rows; r0 += kMaxRowsPerLaunch) {
+    const int64_t n = std::min(rows - r0, kMaxRowsPerLaunch);
+    DfaParams d = {};
+    d.trans = trans;
+    d.n_states = n_states;
+    d.dead = dead;
+    d.dead_absorbing = dead_absorbing ? 1 : 0;
+    d.states = states + r0;
+    d.rows = n;
+    d.tok_bytes = tok_bytes;
+    d.n_bytes = n_bytes;
+    d.tok_offsets = tok_offsets;
+    d.vocab = vocab;
+    d.out = out + r0 * out_stride;
+    d.out_stride = out_stride;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((words + kDfaWarpsPerBlock - 1) / kDfaWarpsPerBlock),
+                       (unsigned)((n + kDfaRowsPerWarp - 1) / kDfaRowsPerWarp), 1);
+    cfg.blockDim = dim3(kDfaWarpsPerBlock * 32, 1, 1);
+    cfg.stream = (cudaStream_t)stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    const int rc = finish_launch(cudaLaunchKernelEx(&cfg, dfa_mask_kernel, d));
+    if (rc) return rc;
+  }
+  return ONYX_OK;
 }
 
 size_t onyx_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }

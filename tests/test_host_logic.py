@@ -181,3 +181,22 @@ def test_mask_expansion_multiplies_are_carry_free():
                 b1 = (byte >> (2 * pair + 1)) & 1
                 want.append((0xFFFF if b0 else 0) | (0xFFFF0000 if b1 else 0))
             assert got == want, (byte, above)
+
+
+def test_dfa_mask_host_helpers():
+    from onyx_b200 import dfa_masks
+    data, offsets = dfa_masks.pack_tokens([b"ab", b"", b"c"])
+    assert data.tolist() == [0x61, 0x62, 0x63] and offsets.tolist() == [0, 2, 2, 3]
+    trans = np.zeros((3, 256), np.int32)
+    assert dfa_masks.dead_is_absorbing(trans, 0)
+    trans[0, 7] = 2
+    assert not dfa_masks.dead_is_absorbing(trans, 0)
+    # shape and argument errors are raised on the host, before any device is touched
+    with pytest.raises(ValueError):
+        dfa_masks.DfaMaskBuilder(np.zeros((3, 255), np.int32), 0, [b"a"])
+    with pytest.raises(ValueError):
+        dfa_masks.DfaMaskBuilder(trans, 3, [b"a"])
+    with pytest.raises(ValueError):
+        dfa_masks.DfaMaskBuilder(trans, 0, [])
+    with pytest.raises(ValueError):
+        dfa_masks.DfaMaskBuilder(trans, 0, [b"a"], device="cpu")
