@@ -58,6 +58,9 @@ WORKLOADS = {
                     desc="batch-sharded masked argmax bf16 [128/GPU,256000] at 5% density"),
     "vocab_parallel": dict(rows=1024, vocab=256000,
                            desc="vocabulary-sharded masked argmax bf16 [1024,256000/N] + NCCL all-gather"),
+    "dfa_masks": dict(rows=64, vocab=128256,
+                      desc="mask producer: valid-token masks of every state of a 64-state DFA "
+                           "over 128,256 tokens, u32 [64,4008]"),
 }
 
 
@@ -72,6 +75,9 @@ def bytes_per_row(name: str, world: int = 1) -> float:
         return words * 4 + 4 + v * 2 + 8
     if name == "vocab_parallel":
         return (v * 2 + words * 4) / world + 8 + 8
+    if name == "dfa_masks":  # per state row: its mask words written, plus its share of the
+        # vocabulary read once per step (offsets 8 B/token, about 5 token bytes/token)
+        return words * 4 + 4 + (v * 8 + v * 5) / w["rows"]
     return v * 2 + words * 4 + 8
 
 
@@ -178,6 +184,10 @@ def _cpu_inputs(name: str):
         return workloads.scaling(rows=128)
     if name == "vocab_parallel":
         return workloads.scaling(rows=128)
+    if name == "dfa_masks":
+        rng = workloads.np.random.default_rng(workloads.SEEDS[4])
+        return {"dfa": workloads.synthetic_dfa(rng, WORKLOADS[name]["rows"]),
+                "vocabulary": workloads.synthetic_vocabulary(rng, WORKLOADS[name]["vocab"])}
     raise ValueError(name)
 
 
@@ -199,6 +209,18 @@ def cpu_measure(name: str, budget_s: float, steps: int | None = None, warmup: in
 
         rows_per_call = w["logits_bf16"].shape[0]
         what = "spec verify of 32 entries x 5 rows x 151936 bf16"
+    elif name == "dfa_masks":
+        w = _cpu_inputs(name)
+
+        class _Dfa:  # the oracle's scan reads the table and the dead state
+            trans = w["dfa"]["trans"]
+            dead = w["dfa"]["dead"]
+
+        def run_once():
+            oracle.dfa_table(_Dfa, w["vocabulary"], threads=threads)
+
+        rows_per_call = _Dfa.trans.shape[0]
+        what = f"valid-token table of {rows_per_call} DFA states x {len(w['vocabulary'])} tokens"
     else:
         w = _cpu_inputs(name)
         if name == "table_gather":
@@ -249,7 +271,7 @@ def run_reference(args) -> None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16",
+        "dtype": "u32" if args.workload == "dfa_masks" else "bf16",
         "data": "synthetic (seeded, shapes and distributions of the workload)",
         "config": {"workload": args.workload, "desc": WORKLOADS[args.workload]["desc"]},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
@@ -547,6 +569,113 @@ def run_ours(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_dfa_masks(args) -> None:
+    """Mask producer leg: each step builds the valid-token masks of every state of a
+    synthetic DFA over the vocabulary (one launch). One GPU; N > 1 replicas (weak)."""
+    import torch
+    import torch.distributed as dist
+
+    from onyx_b200 import dfa_masks, workloads
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    spec = WORKLOADS["dfa_masks"]
+    w = _cpu_inputs("dfa_masks")
+    dfa, vocab = w["dfa"], w["vocabulary"]
+    builder = dfa_masks.DfaMaskBuilder(dfa["trans"], dfa["dead"], vocab, device=dev)
+    R = spec["rows"]
+    states = torch.arange(R, dtype=torch.int32, device=dev)
+    out_words = builder.words
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            builder.masks(states)
+    stream.synchronize()
+    chunk = min(args.steps, 1024)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(chunk):
+            builder.masks(states)
+    graph.replay()
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        done = 0
+        with torch.cuda.stream(stream):
+            while done < args.steps:
+                graph.replay()
+                done += chunk
+        end.record(stream)
+        end.synchronize()
+    ms_total = start.elapsed_time(end)
+    t = torch.tensor([ms_total / done], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_step = float(t.item())
+    value = R * world / (ms_per_step / 1e3)
+    peak, peak_kind = _peaks()
+    per_launch = bytes_per_row("dfa_masks") * R
+    achieved = per_launch / (ms_per_step / 1e3) / 1e9
+
+    # end to end: the state ids up, the masks down, every step
+    pinned_states = torch.arange(R, dtype=torch.int32).pin_memory()
+    host_out = torch.empty((R, out_words), dtype=torch.int32).pin_memory()
+    dev_states = torch.empty(R, dtype=torch.int32, device=dev)
+    e2e_steps = min(args.steps, 500)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a.record(stream)
+        for _ in range(e2e_steps):
+            dev_states.copy_(pinned_states, non_blocking=True)
+            host_out.copy_(builder.masks(dev_states), non_blocking=True)
+        b.record(stream)
+    b.synchronize()
+    e2e_value = R * e2e_steps / (a.elapsed_time(b) / 1e3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, threads, sample, _, _ = cpu_measure("dfa_masks", budget_s=args.cpu_seconds)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": "dfa_masks rows/s", "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": done, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u32",
+        "data": "synthetic (seeded 64-state DFA, 20% live transitions; synthetic vocabulary)",
+        "config": {"workload": "dfa_masks", "desc": spec["desc"], "rows_per_step_per_gpu": R,
+                   "parallelism": f"replicas x{world}",
+                   "l2_policy": "inputs (1.7 MB vocabulary) stay in L2 by design: the walk is "
+                                "latency-bound, the output is written once per step",
+                   "timing": "CUDA events on the launching stream, CUDA-graph replay"},
+        "gbs": achieved,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs (of {peak_kind})",
+                     "algorithmic_bytes_per_launch": per_launch},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": R * 4,
+                "d2h_bytes_per_step": R * out_words * 4, "steps": e2e_steps},
+        "cpu_baseline": cpu,
+        "gpu_launches": done,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -565,6 +694,8 @@ def main() -> None:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "dfa_masks":
+        run_dfa_masks(args)
     else:
         run_ours(args)
 

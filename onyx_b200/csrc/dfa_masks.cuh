@@ -5,16 +5,17 @@
 // transition table from s does not end in the dead state. Row r of the output is the
 // packed mask (bit t of word t >> 5, LSB first, tail bits zero) of states[r].
 //
-// One warp builds one 32-token mask word for up to kDfaRowsPerWarp states: each lane walks
-// its token from every one of those states in lockstep, so their table loads (read-only
-// path; a regex DFA of a few hundred states stays in L1) overlap, and a ballot packs the
-// word. When the dead state is absorbing a walk stops at it; otherwise the full token is
+// One warp builds one 32-token mask word for up to kDfaMaxRowsPerWarp states: each lane loads
+// its token once and walks it from kDfaLockstep states at a time in lockstep, so their table
+// loads (read-only path; a regex DFA of a few hundred states stays in L1) overlap, and a
+// ballot packs each row's word. When the dead state is absorbing a walk stops at it; otherwise the full token is
 // walked, which is the reference's final-state rule in both cases. A transition outside
 // the table counts as the dead state and a token whose offsets leave the byte array counts
 // as empty, so malformed input cannot send a load out of bounds; a state id outside the
 // table yields an empty row.
 
-constexpr int kDfaRowsPerWarp = 4;
+constexpr int kDfaMaxRowsPerWarp = 32;  // state rows one warp builds for its token word
+constexpr int kDfaLockstep = 4;         // of which walked together
 constexpr int kDfaWarpsPerBlock = 8;
 constexpr int kDfaCachedBytes = 16;  // token bytes kept in registers; longer tails re-read
 
@@ -31,6 +32,7 @@ struct DfaParams {
   int64_t vocab;
   uint32_t* out;  // [rows][out_stride] words
   int64_t out_stride;
+  int rows_per_warp;  // a multiple of kDfaLockstep, at most kDfaMaxRowsPerWarp
 };
 
 __global__ void __launch_bounds__(kDfaWarpsPerBlock * 32) dfa_mask_kernel(const DfaParams d) {
@@ -39,7 +41,7 @@ __global__ void __launch_bounds__(kDfaWarpsPerBlock * 32) dfa_mask_kernel(const 
   const int64_t word = (int64_t)blockIdx.x * kDfaWarpsPerBlock + (threadIdx.x >> 5);
   const int64_t words = (d.vocab + 31) / 32;
   if (word >= words) return;  // warp-uniform
-  const int64_t row0 = (int64_t)blockIdx.y * kDfaRowsPerWarp;
+  const int64_t row0 = (int64_t)blockIdx.y * d.rows_per_warp;
   const int64_t t = word * 32 + lane;
 
   // this lane's token: length and its first bytes in registers
@@ -56,47 +58,50 @@ __global__ void __launch_bounds__(kDfaWarpsPerBlock * 32) dfa_mask_kernel(const 
   for (int i = 0; i < kDfaCachedBytes; ++i)
     if (i < len) cached[i >> 2] |= (uint32_t)__ldg(d.tok_bytes + a + i) << (8 * (i & 3));
 
-  // the walks, one per state row, in lockstep
-  int32_t s[kDfaRowsPerWarp];
-  bool live[kDfaRowsPerWarp];
+  // the walks, kDfaLockstep state rows at a time, the token bytes reused for all of them
+  const int64_t row_end = min(d.rows, row0 + (int64_t)d.rows_per_warp);
+  for (int64_t rg = row0; rg < row_end; rg += kDfaLockstep) {
+    int32_t s[kDfaLockstep];
+    bool live[kDfaLockstep];
 #pragma unroll
-  for (int j = 0; j < kDfaRowsPerWarp; ++j) {
-    const int64_t r = row0 + j;
-    const int32_t st = r < d.rows ? __ldg(d.states + r) : -1;
-    const bool ok = st >= 0 && st < d.n_states;
-    s[j] = ok ? st : d.dead;
-    live[j] = ok && len > 0 && !(d.dead_absorbing && st == d.dead);
-  }
-  for (int64_t i = 0; i < len; ++i) {
-    bool any = false;
+    for (int j = 0; j < kDfaLockstep; ++j) {
+      const int64_t r = rg + j;
+      const int32_t st = r < row_end ? __ldg(d.states + r) : -1;
+      const bool ok = st >= 0 && st < d.n_states;
+      s[j] = ok ? st : d.dead;
+      live[j] = ok && len > 0 && !(d.dead_absorbing && st == d.dead);
+    }
+    for (int64_t i = 0; i < len; ++i) {
+      bool any = false;
 #pragma unroll
-    for (int j = 0; j < kDfaRowsPerWarp; ++j) any |= live[j];
-    if (!any) break;
-    uint32_t b;
-    if (i < kDfaCachedBytes) {
-      uint32_t w = cached[0];
+      for (int j = 0; j < kDfaLockstep; ++j) any |= live[j];
+      if (!any) break;
+      uint32_t b;
+      if (i < kDfaCachedBytes) {
+        uint32_t w = cached[0];
 #pragma unroll
-      for (int q = 1; q < kDfaCachedBytes / 4; ++q)
-        if ((i >> 2) == q) w = cached[q];
-      b = (w >> (8 * (i & 3))) & 0xFFu;
-    } else {
-      b = __ldg(d.tok_bytes + a + i);
+        for (int q = 1; q < kDfaCachedBytes / 4; ++q)
+          if ((i >> 2) == q) w = cached[q];
+        b = (w >> (8 * (i & 3))) & 0xFFu;
+      } else {
+        b = __ldg(d.tok_bytes + a + i);
+      }
+#pragma unroll
+      for (int j = 0; j < kDfaLockstep; ++j) {
+        if (!live[j]) continue;
+        int32_t nx = __ldg(d.trans + (int64_t)s[j] * 256 + b);
+        if (nx < 0 || nx >= d.n_states) nx = d.dead;  // malformed table: dead, never out of bounds
+        s[j] = nx;
+        if (d.dead_absorbing && nx == d.dead) live[j] = false;
+      }
     }
 #pragma unroll
-    for (int j = 0; j < kDfaRowsPerWarp; ++j) {
-      if (!live[j]) continue;
-      int32_t nx = __ldg(d.trans + (int64_t)s[j] * 256 + b);
-      if (nx < 0 || nx >= d.n_states) nx = d.dead;  // malformed table: dead, never out of bounds
-      s[j] = nx;
-      if (d.dead_absorbing && nx == d.dead) live[j] = false;
+    for (int j = 0; j < kDfaLockstep; ++j) {
+      const int64_t r = rg + j;
+      // rows past the end and state ids outside the table start (and stay) at dead
+      const bool valid = t < d.vocab && len > 0 && s[j] != d.dead;
+      const uint32_t bits = __ballot_sync(kFull, valid);
+      if (lane == 0 && r < row_end) d.out[r * d.out_stride + word] = bits;
     }
-  }
-#pragma unroll
-  for (int j = 0; j < kDfaRowsPerWarp; ++j) {
-    const int64_t r = row0 + j;
-    // rows past the end and state ids outside the table start (and stay) at dead
-    const bool valid = t < d.vocab && len > 0 && s[j] != d.dead;
-    const uint32_t bits = __ballot_sync(kFull, valid);
-    if (lane == 0 && r < d.rows) d.out[r * d.out_stride + word] = bits;
   }
 }

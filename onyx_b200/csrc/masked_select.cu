@@ -1512,7 +1512,13 @@ int onyx_dfa_state_masks(const int32_t* trans, int32_t n_states, int32_t dead,
   if (rows == 0) return ONYX_OK;
   if (!states || !out) return ONYX_ERR_INVALID_ARGUMENT;
   const int64_t words = (vocab + 31) / 32;
-  constexpr int64_t kMaxRowsPerLaunch = (int64_t)65535 * kDfaRowsPerWarp;
+  // the most rows per warp (token bytes loaded once for more walks) that still leaves a few
+  // waves of warps
+  constexpr int64_t kTargetWarps = 28 * 1024;
+  int rpw = kDfaLockstep;
+  while (rpw < kDfaMaxRowsPerWarp && words * ((rows + 2 * rpw - 1) / (2 * rpw)) >= kTargetWarps)
+    rpw *= 2;
+  const int64_t kMaxRowsPerLaunch = (int64_t)65535 * rpw;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -1531,9 +1537,10 @@ int onyx_dfa_state_masks(const int32_t* trans, int32_t n_states, int32_t dead,
     d.vocab = vocab;
     d.out = out + r0 * out_stride;
     d.out_stride = out_stride;
+    d.rows_per_warp = rpw;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)((words + kDfaWarpsPerBlock - 1) / kDfaWarpsPerBlock),
-                       (unsigned)((n + kDfaRowsPerWarp - 1) / kDfaRowsPerWarp), 1);
+                       (unsigned)((n + rpw - 1) / rpw), 1);
     cfg.blockDim = dim3(kDfaWarpsPerBlock * 32, 1, 1);
     cfg.stream = (cudaStream_t)stream;
     cfg.attrs = attr;

@@ -101,6 +101,17 @@ def synthetic_vocabulary(rng: np.random.Generator, size: int = 32000) -> list[by
     return vocab
 
 
+def synthetic_dfa(rng: np.random.Generator, states: int = 64, live: float = 0.2) -> dict:
+    """Dense byte DFA with an absorbing dead state 0 and start state 1: every other
+    (state, byte) transition goes to a uniformly drawn live state with probability `live`,
+    else to dead (a grammar that admits a few bytes per state, like a JSON or number
+    pattern)."""
+    trans = rng.integers(1, states, size=(states, 256), dtype=np.int32)
+    trans[rng.random((states, 256)) >= live] = 0
+    trans[0, :] = 0
+    return {"trans": trans, "dead": 0, "start": 1}
+
+
 def single_row(seed: int = SEEDS[1]) -> dict:
     rng = np.random.default_rng(seed)
     vocabulary = synthetic_vocabulary(rng, 32000)
