@@ -14,6 +14,7 @@ Python boundary kept as a drop-in:
 """
 
 from . import bitmask
+from .dfa_masks import DfaMaskBuilder
 from ._lib import OnyxCallError, OnyxError, OnyxLibraryUnavailableError
 from .masked_selection import (
     STATUS_ALL_NEG_INF,
@@ -55,4 +56,5 @@ __all__ = [
     "STATUS_NAN_IN_SUPPORT",
     "STATUS_BAD_STATE",
     "STATUS_WAIT_TIMEOUT",
+    "DfaMaskBuilder",
 ]
