@@ -12,6 +12,12 @@ Run once in a container that holds the reference checkout (read-only) at
   generation.py:212-224) over rows masked the way the reference's list masks do
   (onyx_cuda/tests/test_grammar_selection.py:791-798), including the edge rows of the
   CUDA mask tests (onyx_cuda/tests/test_torch_grammar_mask.py:650-809).
+* ``sampling_cases.json`` -- the kept ids and probabilities of temperature / top-p
+  sampling computed by the reference's ``_filtered_reference_weights``
+  (onyx_cuda/src/onyx_cuda/selection.py, the distribution behind
+  ``create_reference_sampler``) over masked rows (invalid ids -inf, as mask.apply leaves
+  them); an empty valid set or an all -inf support is the mask's rejection
+  (torch_grammar_mask.py:182-185), NaN the sampler's.
 * ``verify_cases.json`` -- grammar-aware speculative verification outcomes computed by
   ``decide_grammar_masked_target_acceptance`` (grammar_acceptance.py:166) and
   ``decide_grammar_masked_post_acceptance_continuation`` (grammar_continuation.py:102)
@@ -42,6 +48,11 @@ from onyx_cuda.grammar_continuation import (  # noqa: E402
 )
 from onyx_cuda.testing import FakeGrammarConstraint, FakeGrammarProgram  # noqa: E402
 from regex_parity_fixtures import REGEX_PARITY_CASES  # noqa: E402
+from onyx_cuda.selection import (  # noqa: E402
+    SamplingDistributionError,
+    TemperatureTopPSelection,
+    _filtered_reference_weights,
+)
 
 OUT = Path(__file__).resolve().parent
 
@@ -380,12 +391,69 @@ def verify_fixtures(rng: np.random.Generator) -> dict:
     return {"cases": cases}
 
 
+def _reference_kept(row_values: list[float], valid: list[int], temperature: float,
+                    top_p: float):
+    if not valid:
+        return "empty_mask", []
+    masked = _list_mask(row_values, set(valid))
+    if all(masked[i] == -math.inf for i in valid):
+        return "all_neg_inf", []
+    policy = TemperatureTopPSelection(temperature=temperature, top_p=top_p, seed=0)
+    try:
+        kept = _filtered_reference_weights(masked, policy)
+    except SamplingDistributionError:
+        return "nan_in_support", []
+    return "ok", [[int(t), float(p).hex()] for t, p in kept]
+
+
+def sampling_fixtures(rng: np.random.Generator) -> dict:
+    cases = []
+    policies = [(1.0, 1.0), (0.8, 0.9), (0.5, 0.5), (2.0, 0.95), (1.3, 0.05), (0.7, 1.0)]
+    for n in range(36):
+        vocab = int(rng.integers(40, 400))
+        dtype = "bf16" if n % 3 else "f32"
+        row = (rng.standard_normal(vocab) * 3.0).astype(np.float32)
+        valid = sorted(int(i) for i in np.flatnonzero(rng.random(vocab) < rng.uniform(0.05, 0.6)))
+        kind = n % 9
+        if kind == 1 and valid:  # exact ties among the leaders
+            row[valid[: min(4, len(valid))]] = row.max() + 1.0
+        elif kind == 2 and valid:  # +inf among the valid ids, and outside them
+            row[valid[0]] = np.inf
+            row[valid[-1]] = np.inf
+            row[0] = np.inf
+        elif kind == 3 and valid:  # NaN valid
+            row[valid[len(valid) // 2]] = np.nan
+        elif kind == 4:  # NaN outside the valid set only
+            row[[i for i in range(vocab) if i not in set(valid)][:3]] = np.nan
+        elif kind == 5 and valid:  # all valid -inf
+            row[valid] = -np.inf
+        elif kind == 6:
+            valid = []
+        elif kind == 7 and valid:  # one valid id
+            valid = valid[:1]
+        elif kind == 8 and valid:  # some valid -inf, flat values
+            row[:] = 0.25
+            row[valid[::2]] = -np.inf
+        bits = _float_bits(row, dtype)
+        values = _bits_to_floats(bits, dtype)
+        temperature, top_p = policies[n % len(policies)]
+        status, kept = _reference_kept(values, valid, temperature, top_p)
+        cases.append({
+            "name": f"sample_{n:02d}_kind{kind}", "dtype": dtype, "bits": bits,
+            "mask_words": _mask_words(valid, vocab), "temperature": temperature,
+            "top_p": top_p, "expected_status": status, "expected_kept": kept,
+        })
+    return {"source": "onyx_cuda/src/onyx_cuda/selection.py _filtered_reference_weights",
+            "cases": cases}
+
+
 def main() -> None:
     rng = np.random.default_rng(20260714)
     files = {
         "regex_parity.json": regex_fixtures(),
         "selection_cases.json": selection_fixtures(rng),
         "verify_cases.json": verify_fixtures(rng),
+        "sampling_cases.json": sampling_fixtures(rng),
     }
     for name, payload in files.items():
         payload["generator"] = "tests/golden/make_golden.py"

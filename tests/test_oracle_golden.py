@@ -99,3 +99,38 @@ def test_delayed_match_quirk_for_single_row_grammar():
     assert dfa.valid_token_ids(dfa.start, vocab) == (0, 1, 2, 3, 8)
     assert not dfa.is_match_state(dfa.start)
     assert dfa.is_match_state(dfa.walk(dfa.start, b"12"))
+
+
+SAMPLING = load_golden("sampling_cases.json")["cases"]
+
+
+def _float_row(case) -> np.ndarray:
+    vals = golden_values(case["bits"], case["dtype"])
+    if case["dtype"] == "bf16":
+        return (vals.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    return vals.astype(np.float64)
+
+
+@pytest.mark.parametrize("case", SAMPLING, ids=[c["name"] for c in SAMPLING])
+def test_sampling_oracle_matches_reference_filtering(case):
+    """Kept ids and probabilities (bit for bit) of the reference's _filtered_reference_weights."""
+    from oracle import sampling
+
+    row = _float_row(case)
+    valid = sampling.unpack_mask(np.asarray(case["mask_words"], np.uint32), row.size)
+    status, kept = sampling.kept_weights(row, valid, case["temperature"], case["top_p"])
+    names = {0: "ok", 1: "empty_mask", 2: "all_neg_inf", 4: "nan_in_support"}
+    assert names[status] == case["expected_status"]
+    assert [[t, p.hex()] for t, p in kept] == case["expected_kept"]
+
+
+def test_philox_known_answers():
+    """Philox4x32-10 against the published known-answer vectors of its authors' library."""
+    from oracle.sampling import philox4x32_10
+
+    assert philox4x32_10((0, 0, 0, 0), (0, 0)) == (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)
+    assert philox4x32_10((0xFFFFFFFF,) * 4, (0xFFFFFFFF, 0xFFFFFFFF)) == (
+        0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)
+    assert philox4x32_10((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344),
+                         (0xA4093822, 0x299F31D0)) == (0xD16CFE09, 0x94FDCCEB, 0x5001E420,
+                                                       0x24126EA1)
