@@ -154,6 +154,23 @@ ONYX_API int onyx_combine_partials(const uint64_t* keys, int64_t n_parts, int64_
                           uint32_t* out_status, void* stream);
 
 /*
+ * Masked temperature / top-p sampling, one draw per row. The distribution and the kept
+ * (top-p) set are the reference's (onyx_cuda/src/onyx_cuda/selection.py,
+ * _filtered_reference_weights, float64): over the valid ids, any +inf shares the mass
+ * equally among the +inf ids, else weights exp((v - max) / temperature); ranked by
+ * (-probability, id), the shortest prefix reaching top_p is kept. The draw of row r is
+ * Philox4x32-10 with key `seed` and counter (call, r), as a 53-bit double u; the sampled id
+ * is the first kept id in id order whose cumulative kept probability exceeds u times the
+ * kept total. Same arguments, same outputs. Status bits as for onyx_masked_argmax
+ * (EMPTY_MASK, ALL_NEG_INF, NAN_IN_SUPPORT; the id is -1 with any of them).
+ * temperature finite and > 0, 0 < top_p <= 1; bf16 / f16 / f32.
+ */
+ONYX_API int onyx_masked_sample(const void* logits, int dtype, int64_t rows, int64_t vocab,
+                                int64_t row_stride, const uint32_t* mask, int64_t mask_stride,
+                                double temperature, double top_p, uint64_t seed, uint64_t call,
+                                int32_t* out_idx, uint32_t* out_status, void* stream);
+
+/*
  * Valid-token bitmasks of DFA states (the mask producer): row r of `out` (out_stride >=
  * ceil(vocab/32) words) is the packed mask of states[r] -- bit t set iff token t is
  * non-empty and walking its bytes through `trans` ([n_states][256] next-state ids) from

@@ -15,6 +15,7 @@ Python boundary kept as a drop-in:
 
 from . import bitmask
 from .dfa_masks import DfaMaskBuilder
+from .sampling import TemperatureTopPSelection, create_cuda_sampler, masked_sample
 from ._lib import OnyxCallError, OnyxError, OnyxLibraryUnavailableError
 from .masked_selection import (
     STATUS_ALL_NEG_INF,
@@ -57,4 +58,7 @@ __all__ = [
     "STATUS_BAD_STATE",
     "STATUS_WAIT_TIMEOUT",
     "DfaMaskBuilder",
+    "TemperatureTopPSelection",
+    "create_cuda_sampler",
+    "masked_sample",
 ]

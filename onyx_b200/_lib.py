@@ -57,6 +57,9 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "onyx_combine_partials": (_i32, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "onyx_masked_argmax_noalloc": (
         _i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
+    "onyx_masked_sample": (
+        _i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, ctypes.c_double, ctypes.c_double,
+               ctypes.c_uint64, ctypes.c_uint64, _vp, _vp, _vp]),
     "onyx_dfa_state_masks": (
         _i32, [_vp, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp]),
     "onyx_ipc_handle_bytes": (_sz, []),

@@ -1083,6 +1083,7 @@ __global__ void combine_keys_kernel(const unsigned long long* keys, int64_t n_pa
 
 #include "peer_exchange.cuh"
 #include "dfa_masks.cuh"
+#include "masked_sample.cuh"
 
 // ---------------------------------------------------------------------------------------
 // host side
@@ -1499,6 +1500,50 @@ int onyx_vocab_partial_argmax(const void* logits, int dtype, int64_t rows, int64
   rc = bind_workspace(p, workspace, workspace_bytes, workspace_bytes_for(rows, rows, pl, 1), rows);
   if (rc) return rc;
   return finish_launch(dispatch<kModeKey>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled()));
+}
+
+int onyx_masked_sample(const void* logits, int dtype, int64_t rows, int64_t vocab,
+                       int64_t row_stride, const uint32_t* mask, int64_t mask_stride,
+                       double temperature, double top_p, uint64_t seed, uint64_t call,
+                       int32_t* out_idx, uint32_t* out_status, void* stream) {
+  if (dtype != kF32 && dtype != kF16 && dtype != kBF16) return ONYX_ERR_UNSUPPORTED_DTYPE;
+  if (rows < 0 || rows > 0x7FFFFFFFll || vocab <= 0 || vocab > 0x7FFFFFFFll - 1)
+    return ONYX_ERR_INVALID_ARGUMENT;
+  if (!(temperature > 0.0) || !(temperature < INFINITY) || !(top_p > 0.0) || !(top_p <= 1.0))
+    return ONYX_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return ONYX_OK;
+  if (!logits || !out_idx || !out_status || (row_stride < vocab && rows > 1))
+    return ONYX_ERR_INVALID_ARGUMENT;
+  if (mask && mask_stride < (vocab + 31) / 32 && rows > 1) return ONYX_ERR_INVALID_ARGUMENT;
+  SampleParams sp = {};
+  sp.logits = logits;
+  sp.row_stride = row_stride;
+  sp.vocab = vocab;
+  sp.mask = mask;
+  sp.mask_stride = mask_stride;
+  sp.temperature = temperature;
+  sp.top_p = top_p;
+  sp.seed = seed;
+  sp.call = call;
+  sp.rows = rows;
+  sp.out_idx = out_idx;
+  sp.out_status = out_status;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)rows, 1, 1);
+  cfg.blockDim = dim3(kSampleThreads, 1, 1);
+  cfg.stream = (cudaStream_t)stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaError_t e;
+  switch (dtype) {
+    case kBF16: e = cudaLaunchKernelEx(&cfg, masked_sample_kernel<kBF16>, sp); break;
+    case kF16: e = cudaLaunchKernelEx(&cfg, masked_sample_kernel<kF16>, sp); break;
+    default: e = cudaLaunchKernelEx(&cfg, masked_sample_kernel<kF32>, sp); break;
+  }
+  return finish_launch(e);
 }
 
 int onyx_dfa_state_masks(const int32_t* trans, int32_t n_states, int32_t dead,
