@@ -153,30 +153,193 @@ __device__ __forceinline__ uint32_t block_sum_u32(uint32_t v, uint32_t* s_u) {
   return r;
 }
 
+// Element loops with kSampleUnroll independent loads in flight per thread (the value and its
+// mask word are loaded side by side). f(i, v) sees the valid ids only.
+constexpr int kSampleUnroll = 8;
+
+template <int DT, class F>
+__device__ __forceinline__ void for_each_strided(const void* rowp, const uint32_t* mrow,
+                                                 int64_t V, F f, bool vec) {
+  int64_t start = 0;
+  if (vec) {
+    // 16-byte vectors: E elements per lane per load, E mask bits from one word (vector
+    // starts are multiples of E, so the E bits never straddle two words)
+    constexpr int E = 16 / (int)sizeof(typename Elem<DT>::storage);
+    const int64_t nvec = V / E;
+    const uint4* vp = static_cast<const uint4*>(rowp);
+    for (int64_t b = threadIdx.x; b < nvec; b += (int64_t)kSampleThreads * 2) {
+      uint4 x[2];
+      uint32_t bits[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int64_t vi = b + (int64_t)k * kSampleThreads;
+        const bool in = vi < nvec;
+        x[k] = in ? __ldg(vp + vi) : make_uint4(0u, 0u, 0u, 0u);
+        const int64_t e = vi * E;
+        bits[k] = !in ? 0u : !mrow ? 0xFFu : (__ldg(mrow + (e >> 5)) >> (e & 31)) & ((1u << E) - 1u);
+      }
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int64_t e = (b + (int64_t)k * kSampleThreads) * E;
+        const uint32_t w[4] = {x[k].x, x[k].y, x[k].z, x[k].w};
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+          if (!((bits[k] >> j) & 1u)) continue;
+          float v;
+          if constexpr (DT == kF32) {
+            v = __uint_as_float(w[j]);
+          } else {
+            const uint32_t h = (w[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;
+            v = DT == kBF16 ? bf16_bits_to_f32(h) : f16_bits_to_f32(h);
+          }
+          f(e + j, v);
+        }
+      }
+    }
+    start = nvec * E;
+  }
+  for (int64_t base = start + threadIdx.x; base < V;
+       base += (int64_t)kSampleThreads * kSampleUnroll) {
+    float v[kSampleUnroll];
+    bool ok[kSampleUnroll];
+#pragma unroll
+    for (int k = 0; k < kSampleUnroll; ++k) {
+      const int64_t i = base + (int64_t)k * kSampleThreads;
+      const bool in = i < V;
+      v[k] = in ? sample_value<DT>(rowp, i) : 0.f;
+      ok[k] = in && sample_valid(mrow, i);
+    }
+#pragma unroll
+    for (int k = 0; k < kSampleUnroll; ++k)
+      if (ok[k]) f(base + (int64_t)k * kSampleThreads, v[k]);
+  }
+}
+
+// The valid ids of [lo, hi) in increasing order; f(i, v) returns true to stop.
+template <int DT, class F>
+__device__ __forceinline__ void for_each_in_range(const void* rowp, const uint32_t* mrow,
+                                                  int64_t lo, int64_t hi, F f) {
+  for (int64_t base = lo; base < hi; base += kSampleUnroll) {
+    float v[kSampleUnroll];
+    bool ok[kSampleUnroll];
+#pragma unroll
+    for (int k = 0; k < kSampleUnroll; ++k) {
+      const int64_t i = base + k;
+      const bool in = i < hi;
+      v[k] = in ? sample_value<DT>(rowp, i) : 0.f;
+      ok[k] = in && sample_valid(mrow, i);
+    }
+#pragma unroll
+    for (int k = 0; k < kSampleUnroll; ++k)
+      if (ok[k] && f(base + k, v[k])) return;
+  }
+}
+
+// Warp-range iteration with compaction: warp w owns the contiguous ids [w R, (w + 1) R)
+// (R a multiple of 8). In steps of 256 ids (8 per lane, one 16-byte load for 16-bit types
+// when the row is aligned), the ids that pred(i, v) keeps are packed, in id order, into the
+// warp's shared-memory buffer and handed to batch(has, i, v) 32 at a time, one per lane, so
+// that the per-id work (a float64 exp) runs on full warps however sparse the kept ids are.
+// batch is called by every lane of the warp (has = this lane holds an id) and may use warp
+// collectives; it returns true (warp-uniformly) to stop the walk.
+constexpr int kSampleStep = 256;  // ids per warp step: 8 per lane
+
+struct WarpBuf {
+  float v[kSampleStep];
+  uint16_t off[kSampleStep];  // id - step base
+};
+
+template <int DT, class Pred, class Batch>
+__device__ __forceinline__ void warp_range_batches(const void* rowp, const uint32_t* mrow,
+                                                   int64_t lo, int64_t hi, bool vec,
+                                                   WarpBuf* buf, Pred pred, Batch batch) {
+  using St = typename Elem<DT>::storage;
+  const int lane = threadIdx.x & 31;
+  for (int64_t base = lo; base < hi; base += kSampleStep) {
+    const int64_t e0 = base + 8 * lane;
+    float v[8];
+    uint32_t keep = 0u;
+    const uint32_t word = e0 < hi && mrow ? __ldg(mrow + (e0 >> 5)) >> (e0 & 31) : 0xFFu;
+    if (vec && e0 + 8 <= hi) {
+      if constexpr (DT == kF32) {
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(static_cast<const St*>(rowp) + e0));
+        const uint4 b = __ldg(reinterpret_cast<const uint4*>(static_cast<const St*>(rowp) + e0) + 1);
+        const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(w[j]);
+      } else {
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(static_cast<const St*>(rowp) + e0));
+        const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t h = (w[j >> 1] >> (16 * (j & 1))) & 0xFFFFu;
+          v[j] = DT == kBF16 ? bf16_bits_to_f32(h) : f16_bits_to_f32(h);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = e0 + j < hi ? sample_value<DT>(rowp, e0 + j) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (e0 + j < hi && ((word >> j) & 1u) && pred(e0 + j, v[j])) keep |= 1u << j;
+    // pack the kept ids in id order (lane-major, then j)
+    const uint32_t cnt = __popc(keep);
+    uint32_t incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t n = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += n;
+    }
+    const uint32_t total = __shfl_sync(kFull, incl, 31);
+    uint32_t pos = incl - cnt;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if ((keep >> j) & 1u) {
+        buf->v[pos] = v[j];
+        buf->off[pos] = (uint16_t)(8 * lane + j);
+        ++pos;
+      }
+    }
+    __syncwarp();
+    bool stop = false;
+    for (uint32_t k = 0; k < total && !stop; k += 32) {
+      const bool has = k + lane < total;
+      stop = batch(has, has ? base + buf->off[k + lane] : (int64_t)-1,
+                   has ? buf->v[k + lane] : 0.f);  // warp-uniform
+    }
+    __syncwarp();
+    if (stop) return;
+  }
+}
+
 // Id of the n-th (0-based) id of the row, in increasing id order, for which pred(i) holds,
 // or -1. Threads own contiguous id ranges; a block scan of their counts finds the owner.
-template <class Pred>
-__device__ int64_t block_nth_id(int64_t V, int64_t n, Pred pred, double* s_red,
-                                long long* s_found) {
+template <int DT, class Pred>
+__device__ int64_t block_nth_id(const void* rowp, const uint32_t* mrow, int64_t V, int64_t n,
+                                Pred pred, double* s_red, long long* s_found) {
   const int64_t chunk = (V + kSampleThreads - 1) / kSampleThreads;
   const int64_t lo = min(V, (int64_t)threadIdx.x * chunk), hi = min(V, lo + chunk);
   int64_t cnt = 0;
-  for (int64_t i = lo; i < hi; ++i) cnt += pred(i) ? 1 : 0;
+  for_each_in_range<DT>(rowp, mrow, lo, hi, [&](int64_t i, float v) {
+    cnt += pred(i, v) ? 1 : 0;
+    return false;
+  });
   double total;
   const int64_t before = (int64_t)block_exclusive_scan_d((double)cnt, s_red, &total);
   if (threadIdx.x == 0) *s_found = -1;
   __syncthreads();
   if (n >= before && n < before + cnt) {
     int64_t k = before;
-    for (int64_t i = lo; i < hi; ++i) {
-      if (pred(i)) {
-        if (k == n) {
-          *s_found = i;
-          break;
-        }
-        ++k;
+    for_each_in_range<DT>(rowp, mrow, lo, hi, [&](int64_t i, float v) {
+      if (!pred(i, v)) return false;
+      if (k == n) {
+        *s_found = i;
+        return true;
       }
-    }
+      ++k;
+      return false;
+    });
   }
   __syncthreads();
   const int64_t r = *s_found;
@@ -184,10 +347,16 @@ __device__ int64_t block_nth_id(int64_t V, int64_t n, Pred pred, double* s_red,
   return r;
 }
 
+// dynamic shared memory: the warps' compaction buffers, reused for the histograms
+constexpr size_t kSampleSmemBytes = sizeof(WarpBuf) * kSampleWarps;
+static_assert(kSampleSmemBytes >= kSampleBins * (sizeof(double) + sizeof(uint32_t)), "");
+
 template <int DT>
 __global__ void __launch_bounds__(kSampleThreads) masked_sample_kernel(const SampleParams p) {
-  __shared__ double s_mass[kSampleBins];
-  __shared__ uint32_t s_count[kSampleBins];
+  extern __shared__ __align__(16) unsigned char s_dyn[];
+  WarpBuf* const s_bufs = reinterpret_cast<WarpBuf*>(s_dyn);
+  double* const s_mass = reinterpret_cast<double*>(s_dyn);
+  uint32_t* const s_count = reinterpret_cast<uint32_t*>(s_dyn + kSampleBins * sizeof(double));
   __shared__ double s_red[kSampleWarps];
   __shared__ uint32_t s_u[kSampleWarps];
   __shared__ uint32_t s_bin;
@@ -200,13 +369,12 @@ __global__ void __launch_bounds__(kSampleThreads) masked_sample_kernel(const Sam
   using St = typename Elem<DT>::storage;
   const void* rowp = static_cast<const St*>(p.logits) + row * p.row_stride;
   const uint32_t* mrow = p.mask ? p.mask + row * p.mask_stride : nullptr;
+  const bool vec = ((uintptr_t)rowp & 15u) == 0;  // 16-byte loads (block-uniform)
 
   // 1. support: any valid id, NaN, +inf count, the largest finite value (as an order code)
   uint32_t any = 0u, nan = 0u, pinf = 0u, maxo = 0u;
-  for (int64_t i = tid; i < V; i += kSampleThreads) {
-    if (!sample_valid(mrow, i)) continue;
+  for_each_strided<DT>(rowp, mrow, V, [&](int64_t, float v) {
     any = 1u;
-    const float v = sample_value<DT>(rowp, i);
     if (v != v) {
       nan = 1u;
     } else if (v == INFINITY) {
@@ -214,7 +382,7 @@ __global__ void __launch_bounds__(kSampleThreads) masked_sample_kernel(const Sam
     } else if (v != -INFINITY) {
       maxo = max(maxo, ord32(v));
     }
-  }
+  }, vec);
   any = block_or_u32(any, s_u);
   nan = block_or_u32(nan, s_u);
   pinf = block_sum_u32(pinf, s_u);
@@ -261,10 +429,8 @@ __global__ void __launch_bounds__(kSampleThreads) masked_sample_kernel(const Sam
     }
     __syncthreads();
     const int64_t pick = s_pick;
-    const int64_t id = block_nth_id(
-        V, pick,
-        [&](int64_t i) { return sample_valid(mrow, i) && sample_value<DT>(rowp, i) == INFINITY; },
-        s_red, &s_found);
+    const int64_t id = block_nth_id<DT>(
+        rowp, mrow, V, pick, [&](int64_t, float v) { return v == INFINITY; }, s_red, &s_found);
     if (tid == 0) {
       p.out_idx[row] = (int32_t)id;
       p.out_status[row] = 0u;
@@ -277,55 +443,64 @@ __global__ void __launch_bounds__(kSampleThreads) masked_sample_kernel(const Sam
   // divide by T, as the reference does: multiplying by 1/T rounds differently
   auto weight_exact = [&](float v) { return exp(((double)v - vmax) / p.temperature); };
 
-  // 3. total mass and the first radix level (order-code bits 31..21) in one pass
-  for (int b = tid; b < kSampleBins; b += kSampleThreads) {
-    s_mass[b] = 0.0;
-    s_count[b] = 0u;
-  }
-  __syncthreads();
+  // 3. total mass and the number of weighted ids
+  const int warp = tid >> 5, lane = tid & 31;
+  const int64_t wrange = ((V + 31) / 32 + 7) / 8 * 8;  // each warp's ids, a multiple of 8
+  const int64_t wlo = min(V, (int64_t)warp * wrange), whi = min(V, wlo + wrange);
   double tsum = 0.0;
-  for (int64_t i = tid; i < V; i += kSampleThreads) {
-    if (!sample_valid(mrow, i)) continue;
-    const float v = sample_value<DT>(rowp, i);
-    if (v == -INFINITY) continue;
-    const double w = weight_exact(v);
-    if (!(w > 0.0)) continue;
-    tsum += w;
-    const uint32_t b = ord32(v) >> 21;
-    atomicAdd(&s_mass[b], w);
-    atomicAdd(&s_count[b], 1u);
-  }
+  uint32_t nw = 0u;
+  warp_range_batches<DT>(
+      rowp, mrow, wlo, whi, vec, &s_bufs[warp], [&](int64_t, float v) { return v != -INFINITY; },
+      [&](bool has, int64_t, float v) {
+        if (has) {
+          const double w = weight_exact(v);
+          if (w > 0.0) {
+            tsum += w;
+            ++nw;
+          }
+        }
+        return false;
+      });
+  __syncthreads();  // the buffers become the histograms
   const double total = block_sum_d(tsum, s_red);
+  nw = block_sum_u32(nw, s_u);
+  // The first radix level only needs the ids that can hold the cut: those of weight below
+  // tau = (1 - top_p) total / (2 nw) weigh at most (1 - top_p) total / 2 together, so the
+  // ids above tau reach top_p by themselves. (This keeps the shared-memory histogram from
+  // taking one atomic per id of the row, most of them on a few hot bins.)
+  const double tau = (1.0 - p.top_p) * total / (2.0 * (double)nw);
+  // the same cut on the value, tested before any exp: w >= tau iff v >= max + T ln(tau)
+  const double vtau = tau > 0.0 ? vmax + p.temperature * log(tau) : -INFINITY;
 
-  // 4. levels: find the bin where the probability mass ranked above reaches top_p
+  // 4. levels: find the bin where the probability mass ranked above reaches top_p. With
+  //    top_p = 1 every weighted id is kept: no cut to find.
   double above = 0.0;  // probability of every token ranked above the current prefix
   uint32_t prefix = 0u;
+  const bool keep_all = !(p.top_p < 1.0);
 #pragma unroll
   for (int level = 0; level < 3; ++level) {
+    if (keep_all) break;  // block-uniform
     const int shift = level == 0 ? 21 : level == 1 ? 10 : 0;
     const int width = level == 2 ? 10 : 11;
     const int nb = 1 << width;
-    if (level > 0) {
-      for (int b = tid; b < kSampleBins; b += kSampleThreads) {
-        s_mass[b] = 0.0;
-        s_count[b] = 0u;
-      }
-      __syncthreads();
-      const int pshift = level == 1 ? 21 : 10;
-      for (int64_t i = tid; i < V; i += kSampleThreads) {
-        if (!sample_valid(mrow, i)) continue;
-        const float v = sample_value<DT>(rowp, i);
-        if (v == -INFINITY) continue;
-        const uint32_t o = ord32(v);
-        if ((o >> pshift) != prefix) continue;
-        const double w = weight_exact(v);
-        if (!(w > 0.0)) continue;
-        const uint32_t b = (o >> shift) & (uint32_t)(nb - 1);
-        atomicAdd(&s_mass[b], w);
-        atomicAdd(&s_count[b], 1u);
-      }
-      __syncthreads();
+    for (int b = tid; b < kSampleBins; b += kSampleThreads) {
+      s_mass[b] = 0.0;
+      s_count[b] = 0u;
     }
+    __syncthreads();
+    const int pshift = level == 1 ? 21 : 10;  // the previous level's shift (unused at level 0)
+    for_each_strided<DT>(rowp, mrow, V, [&](int64_t, float v) {
+      if (v == -INFINITY) return;
+      const uint32_t o = ord32(v);
+      if (level > 0 && (o >> pshift) != prefix) return;
+      if (level == 0 && (double)v < vtau) return;
+      const double w = weight_exact(v);
+      if (!(w > 0.0)) return;
+      const uint32_t b = (o >> shift) & (uint32_t)(nb - 1);
+      atomicAdd(&s_mass[b], w);
+      atomicAdd(&s_count[b], 1u);
+    }, vec);
+    __syncthreads();
     // thread t owns bins nb-1-2t and nb-2-2t: a scan in descending bin order
     const int b_hi = nb - 1 - 2 * tid, b_lo = b_hi - 1;
     const double p_hi = b_hi >= 0 ? s_mass[b_hi] / total : 0.0;
@@ -367,10 +542,10 @@ __global__ void __launch_bounds__(kSampleThreads) masked_sample_kernel(const Sam
   }
   // prefix is now the exact order code v* of the value the cut falls on; s_count[bin] of
   // the last level counts its ties
-  const uint32_t vstar = prefix;
-  const uint32_t ties = s_count[vstar & 1023u];
+  const uint32_t vstar = keep_all ? 0u : prefix;  // 0: below every value's code
+  const uint32_t ties = keep_all ? 0u : s_count[vstar & 1023u];
   const float vstar_f = __uint_as_float((vstar & 0x80000000u) ? (vstar & 0x7FFFFFFFu) : ~vstar);
-  const double pstar = weight_exact(vstar_f) / total;
+  const double pstar = keep_all ? 0.0 : weight_exact(vstar_f) / total;
   __shared__ long long s_take;
   if (tid == 0) {
     double cum = above;
@@ -387,61 +562,77 @@ __global__ void __launch_bounds__(kSampleThreads) masked_sample_kernel(const Sam
   __syncthreads();
   const int64_t take = s_take;
   // the last kept tie, in id order
-  const int64_t last_tie = block_nth_id(
-      V, take - 1,
-      [&](int64_t i) {
-        return sample_valid(mrow, i) && ord32(sample_value<DT>(rowp, i)) == vstar;
-      },
-      s_red, &s_found);
+  const int64_t last_tie =
+      keep_all ? V
+               : block_nth_id<DT>(
+                     rowp, mrow, V, take - 1, [&](int64_t, float v) { return ord32(v) == vstar; },
+                     s_red, &s_found);
 
   // 5. the draw: walk the kept ids (ranked at or above the last kept tie) in id order
-  auto kept = [&](int64_t i, double* pi) -> bool {
-    if (!sample_valid(mrow, i)) return false;
-    const float v = sample_value<DT>(rowp, i);
+  auto kept = [&](int64_t i, float v) {
     if (v == -INFINITY) return false;
     const uint32_t o = ord32(v);
-    if (o < vstar || (o == vstar && i > last_tie)) return false;
-    *pi = weight_exact(v) / total;
-    return true;
+    return o > vstar || (o == vstar && i <= last_tie);
   };
-  const int64_t chunk = (V + kSampleThreads - 1) / kSampleThreads;
-  const int64_t lo = min(V, (int64_t)tid * chunk), hi = min(V, lo + chunk);
-  double local = 0.0;
-  long long last_kept = -1;
-  for (int64_t i = lo; i < hi; ++i) {
-    double pi;
-    if (kept(i, &pi)) {
-      local += pi;
-      last_kept = i;
-    }
+  __syncthreads();  // the histograms become the buffers again
+  double wsum = 0.0;       // this warp's kept mass (same in every lane)
+  uint32_t wlast = 0u;     // 1 + the warp's last kept id of positive probability, or 0
+  warp_range_batches<DT>(rowp, mrow, wlo, whi, vec, &s_bufs[warp], kept,
+                         [&](bool has, int64_t i, float v) {
+                           const double pi = has ? weight_exact(v) / total : 0.0;
+                           wsum += warp_sum_d(pi);
+                           wlast = max(wlast, __reduce_max_sync(
+                                                  kFull, pi > 0.0 ? (uint32_t)i + 1u : 0u));
+                           return false;
+                         });
+  // warp sums in warp order = id order: every warp gets its exclusive prefix and the total
+  __shared__ double s_wsum[kSampleWarps];
+  if (lane == 0) s_wsum[warp] = wsum;
+  __syncthreads();
+  double pre = s_wsum[lane], incl = pre;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double n = __shfl_up_sync(kFull, incl, o);
+    if (lane >= o) incl += n;
   }
-  double kept_total;
-  const double before = block_exclusive_scan_d(local, s_red, &kept_total);
+  double excl = __shfl_up_sync(kFull, incl, 1);
+  if (lane == 0) excl = 0.0;
+  const double kept_total = __shfl_sync(kFull, incl, 31);
+  const double before = __shfl_sync(kFull, excl, warp);
+  (void)pre;
   const double threshold = u * kept_total;
   __shared__ unsigned long long s_pick_id;
   if (tid == 0) s_pick_id = ~0ull;
   __syncthreads();
-  if (last_kept >= 0 && before <= threshold && threshold < before + local) {
-    long long pick = last_kept;  // rounding kept the crossing from showing: the chunk's last
-    double c = before;
-    for (int64_t i = lo; i < hi; ++i) {
-      double pi;
-      if (kept(i, &pi)) {
-        c += pi;
-        if (threshold < c) {
-          pick = i;
-          break;
-        }
-      }
-    }
-    atomicMin(&s_pick_id, (unsigned long long)pick);
+  if (wlast && before <= threshold && threshold < before + wsum) {
+    // this warp's range holds the crossing: walk it again with running sums
+    double cum = before;
+    unsigned long long pick = (unsigned long long)wlast - 1ull;  // if rounding hides it
+    warp_range_batches<DT>(rowp, mrow, wlo, whi, vec, &s_bufs[warp], kept,
+                           [&](bool has, int64_t i, float v) {
+                             const double pi = has ? weight_exact(v) / total : 0.0;
+                             double run = pi;
+#pragma unroll
+                             for (int o = 1; o < 32; o <<= 1) {
+                               const double n = __shfl_up_sync(kFull, run, o);
+                               if (lane >= o) run += n;
+                             }
+                             const unsigned hit =
+                                 __ballot_sync(kFull, has && pi > 0.0 && threshold < cum + run);
+                             if (hit) {
+                               pick = (unsigned long long)__shfl_sync(kFull, i, __ffs(hit) - 1);
+                               return true;
+                             }
+                             cum += __shfl_sync(kFull, run, 31);
+                             return false;
+                           });
+    if (lane == 0) atomicMin(&s_pick_id, pick);
   }
   __syncthreads();
   unsigned long long id = s_pick_id;
   if (id == ~0ull) {
     // the draw lies past the sum (rounding): the last kept id, as the reference returns
-    const uint32_t key = last_kept >= 0 ? (uint32_t)last_kept + 1u : 0u;
-    id = (unsigned long long)block_max_u32(key, s_u) - 1ull;
+    id = (unsigned long long)block_max_u32(wlast, s_u) - 1ull;
   }
   if (tid == 0) {
     p.out_idx[row] = (int32_t)id;

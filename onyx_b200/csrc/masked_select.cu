@@ -1537,7 +1537,27 @@ int onyx_masked_sample(const void* logits, int dtype, int64_t rows, int64_t voca
   cfg.stream = (cudaStream_t)stream;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  cudaError_t e;
+  cfg.dynamicSmemBytes = kSampleSmemBytes;
+  // the compaction buffers take 48 KB of dynamic shared memory: opt in once per device
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return finish_launch(e);
+  {
+    static std::mutex mu;
+    static bool ready[64] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 0 || dev >= 64) return ONYX_ERR_INVALID_ARGUMENT;
+    if (!ready[dev]) {
+      for (const void* fn : {(const void*)masked_sample_kernel<kBF16>,
+                             (const void*)masked_sample_kernel<kF16>,
+                             (const void*)masked_sample_kernel<kF32>}) {
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kSampleSmemBytes);
+        if (e != cudaSuccess) return finish_launch(e);
+      }
+      ready[dev] = true;
+    }
+  }
   switch (dtype) {
     case kBF16: e = cudaLaunchKernelEx(&cfg, masked_sample_kernel<kBF16>, sp); break;
     case kF16: e = cudaLaunchKernelEx(&cfg, masked_sample_kernel<kF16>, sp); break;
