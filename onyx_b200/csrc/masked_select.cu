@@ -741,14 +741,20 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
-// Waits for phase `parity` of `bar` to complete; gives up (false) after `limit_ns`.
-__device__ __noinline__ bool mbar_wait_cluster_bounded(unsigned long long* bar, uint32_t parity,
-                                                       unsigned long long limit_ns) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
+__device__ __noinline__ bool mbar_wait_cluster_slow(unsigned long long* bar, uint32_t parity,
+                                                    unsigned long long limit_ns) {
   const unsigned long long t0 = global_ns();
   while (!mbar_try_wait_cluster(bar, parity))
     if (global_ns() - t0 > limit_ns) return false;
   return true;
+}
+
+// Waits for phase `parity` of `bar` to complete; gives up (false) after `limit_ns`. The
+// first poll is inline: normally the phase is already complete.
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(unsigned long long* bar,
+                                                          uint32_t parity,
+                                                          unsigned long long limit_ns) {
+  return mbar_try_wait_cluster(bar, parity) || mbar_wait_cluster_slow(bar, parity, limit_ns);
 }
 
 // Asynchronous 8-byte store into another CTA's shared memory (both addresses from mapa, in
