@@ -501,8 +501,8 @@ __device__ __forceinline__ Partial reduce_member(Partial* base, int segs, int la
 // Outputs of one group, computed by one warp. `single` is the only partial when a group
 // has a single segment (no workspace).
 template <int MODE, bool IS64>
-__device__ void finalize_group(const ScanParams& p, int64_t group, const Partial* single,
-                               int lane, int parts) {
+__device__ __forceinline__ void finalize_group(const ScanParams& p, int64_t group,
+                                               const Partial* single, int lane, int parts) {
   const int P = p.per_group;
   Partial* base = single ? nullptr : p.ws_part + group * (int64_t)P * parts;
   if constexpr (MODE == kModeArgmax || MODE == kModeKey) {
