@@ -39,7 +39,7 @@ UNIT = "rows/s"
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from an ncu capture of the
 # dominant kernel (profiles/masked_select_batched_bf16.md).
-NCU_TRAFFIC_PER_LAUNCH: dict[str, float | None] = {"batched": 17457408.0}
+NCU_TRAFFIC_PER_LAUNCH: dict[str, float | None] = {"batched": 17458688.0}
 
 FALLBACK_HBM_GBS = 6650.0
 
