@@ -1,0 +1,767 @@
+// Masked temperature / top-p sampling, cluster form (included by masked_select.cu after
+// masked_sample.cuh, inside namespace onyx). Same distribution, top-p set and draw as
+// masked_sample_kernel (the reference's _filtered_reference_weights, selection.py:103-150,
+// and the Philox4x32-10 draw); a different decomposition:
+//
+// * One cluster of k CTAs (k = 1..16) per row. CTA r copies ids [r S, min(V, (r + 1) S)) of
+//   the row, values and mask words, into its shared memory once (cp.async, 16-byte copies
+//   when the row is aligned). Every later pass reads shared memory, so a row costs one HBM
+//   read and the passes run on k SMs at once.
+// * Cluster-wide sums and decisions: each CTA posts its block result in a small mailbox,
+//   the cluster barrier publishes it, and every CTA reads the k mailboxes over distributed
+//   shared memory and combines them in rank order. All CTAs therefore hold bit-identical
+//   totals and take the same branches (the cluster barriers always match up).
+// * The top-p cut. Candidates are the ids of weight at least tau = (1 - top_p) total / (2 n)
+//   (the ids below it weigh at most (1 - top_p) total / 2 together, so the ids above reach
+//   top_p by themselves); in value terms v >= vtau = max + T ln(tau). All candidate order
+//   codes lie between code(vtau) and code(max), so they share the leading bits of those
+//   two codes: the radix select starts below that common prefix, which spreads the
+//   candidates over the bins instead of piling them on the few bins of one exponent. It
+//   stops at the last bit a 16-bit source type can set (bit 16 for bf16, 13 for f16; the
+//   lower bits of the code follow from the sign), where each bin is one exact value: the
+//   last level counts ids per value and its mass is count x weight(value), one exp per
+//   bin. Earlier levels (wide ranges, f32) add per-id weights.
+// * The draw. Per warp (warps own contiguous id ranges; CTA ranks follow id order): the
+//   probability of the kept ids ranked strictly above the cut value, and the count of ids
+//   equal to it (the ties, kept in id order up to the count the cut needs). One exchange
+//   gives every CTA the kept mass before each CTA; the last warp, in id order, whose kept
+//   mass starts at or below u x kept_total walks its range with running sums and writes the
+//   sampled id.
+// Sums over many tokens are tree reductions, so their rounding differs from the reference's
+// sequential sums by a few units in the last place, as in masked_sample_kernel.
+
+constexpr int kCsThreads = 1024;
+constexpr int kCsWarps = kCsThreads / 32;
+constexpr int kCsMaxCluster = 16;
+constexpr int kCsBins = 2048;   // widest radix level (11 bits)
+constexpr int kCsSliceAlign = 256;  // ids per slice are a multiple of this (8 per lane x 32)
+
+struct ClusterSampleParams {
+  const void* logits;
+  int64_t row_stride;  // elements
+  int64_t vocab;
+  const uint32_t* mask;  // nullptr: every id valid
+  int64_t mask_stride;   // words
+  double temperature;
+  double top_p;
+  unsigned long long seed;
+  unsigned long long call;
+  int32_t* out_idx;
+  uint32_t* out_status;
+  int32_t k;      // CTAs per row (the cluster size)
+  int32_t slice;  // ids per CTA, a multiple of kCsSliceAlign
+  // dynamic shared memory carve-up (byte offsets)
+  int32_t off_words;  // staged mask words
+  int32_t off_work;   // warp compaction buffers / local histogram
+  int32_t off_comb;   // this CTA's slice of the combined histogram
+};
+
+// One mailbox per exchange; two, used alternately, so that a CTA may post the next
+// exchange while another still reads the previous one (a barrier separates them).
+struct CsMail {
+  double d[2];
+  uint32_t u[4];
+};
+
+struct CsHist {  // local histogram of one radix level (overlays the compaction buffers)
+  double mass[kCsBins];
+  uint32_t count[kCsBins];
+};
+
+__device__ __forceinline__ void cs_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cs_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// generic address of the same shared-memory object in CTA `rank` of the cluster
+template <class T>
+__device__ __forceinline__ const T* cs_remote(const T* p, uint32_t rank) {
+  unsigned long long out;
+  asm volatile("mapa.u64 %0, %1, %2;" : "=l"(out) : "l"(p), "r"(rank));
+  return reinterpret_cast<const T*>(out);
+}
+
+__device__ __forceinline__ void cs_cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src)
+               : "memory");
+}
+
+__device__ __forceinline__ void cs_cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src)
+               : "memory");
+}
+
+__device__ __forceinline__ void cs_cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// Eight staged ids of one lane, from slice-relative id j0 (a multiple of 8): their values
+// and the bits of those that are valid and below lim (lim <= the slice's id count, so
+// j0 < lim keeps all eight reads inside the staged buffer, whose length is a multiple of 8).
+template <int DT>
+__device__ __forceinline__ uint32_t cs_load8(const unsigned char* vals, const uint32_t* words,
+                                             int j0, int lim, float v[8]) {
+  if (j0 >= lim) {
+#pragma unroll
+    for (int t = 0; t < 8; ++t) v[t] = 0.f;
+    return 0u;
+  }
+  if constexpr (DT == kF32) {
+    const uint4 a = *reinterpret_cast<const uint4*>(vals + (size_t)j0 * 4);
+    const uint4 b = *reinterpret_cast<const uint4*>(vals + (size_t)j0 * 4 + 16);
+    v[0] = __uint_as_float(a.x);
+    v[1] = __uint_as_float(a.y);
+    v[2] = __uint_as_float(a.z);
+    v[3] = __uint_as_float(a.w);
+    v[4] = __uint_as_float(b.x);
+    v[5] = __uint_as_float(b.y);
+    v[6] = __uint_as_float(b.z);
+    v[7] = __uint_as_float(b.w);
+  } else {
+    const uint4 a = *reinterpret_cast<const uint4*>(vals + (size_t)j0 * 2);
+    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const uint32_t h = (w[t >> 1] >> (16 * (t & 1))) & 0xFFFFu;
+      v[t] = DT == kBF16 ? bf16_bits_to_f32(h) : f16_bits_to_f32(h);
+    }
+  }
+  uint32_t m = words ? (words[j0 >> 5] >> (j0 & 31)) & 0xFFu : 0xFFu;
+  const int left = lim - j0;
+  if (left < 8) m &= left > 0 ? (1u << left) - 1u : 0u;
+  return m;
+}
+
+// Warp-range walk over staged ids [lo, hi) (slice-relative, lo a multiple of 8) with
+// compaction: in steps of 256 ids (8 per lane), keep8(j0, v, m) -- called by every lane of
+// the warp, so it may use warp collectives -- returns the bits of the lane's 8 ids to keep;
+// the kept ids are packed in id order into the warp's buffer and handed to
+// batch(has, j, x) 32 at a time, one per lane (the per-id work runs on full warps however
+// sparse the kept ids are). batch is called by every lane and returns true, warp-uniformly,
+// to stop the walk.
+template <int DT, class Keep8, class Batch>
+__device__ __forceinline__ void cs_warp_batches(const unsigned char* vals, const uint32_t* words,
+                                                int lo, int hi, WarpBuf* buf, Keep8 keep8,
+                                                Batch batch) {
+  const int lane = threadIdx.x & 31;
+  for (int s = lo; s < hi; s += kSampleStep) {
+    const int j0 = s + 8 * lane;
+    float v[8];
+    const uint32_t m = cs_load8<DT>(vals, words, j0, hi, v);
+    const uint32_t keep = keep8(j0, v, m);
+    const uint32_t cnt = __popc(keep);
+    uint32_t incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const uint32_t total = __shfl_sync(kFull, incl, 31);
+    uint32_t pos = incl - cnt;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      if ((keep >> t) & 1u) {
+        buf->v[pos] = v[t];
+        buf->off[pos] = (uint16_t)(8 * lane + t);
+        ++pos;
+      }
+    }
+    __syncwarp();
+    bool stop = false;
+    for (uint32_t q = 0; q < total && !stop; q += 32) {
+      const bool has = q + lane < total;
+      stop = batch(has, has ? s + (int)buf->off[q + lane] : -1, has ? buf->v[q + lane] : 0.f);
+    }
+    __syncwarp();
+    if (stop) return;
+  }
+}
+
+__device__ __forceinline__ float cs_code_to_float(uint32_t code) {
+  return __uint_as_float((code & 0x80000000u) ? (code & 0x7FFFFFFFu) : ~code);
+}
+
+// The full 32-bit order code from its bits [rb, 32): below bit rb a 16-bit source value has
+// zero bits, which the code keeps for a non-negative value and inverts for a negative one.
+template <int RB>
+__device__ __forceinline__ uint32_t cs_full_code(uint32_t hi_bits) {
+  if constexpr (RB == 0) {
+    return hi_bits;
+  } else {
+    const uint32_t c = hi_bits << RB;
+    return (c & 0x80000000u) ? c : (c | ((1u << RB) - 1u));
+  }
+}
+
+// position of the (r+1)-th set bit of an 8-bit mask (r < popc(m))
+__device__ __forceinline__ int cs_nth_bit8(uint32_t m, uint32_t r) {
+#pragma unroll
+  for (int t = 0; t < 8; ++t) {
+    if ((m >> t) & 1u) {
+      if (r == 0u) return t;
+      --r;
+    }
+  }
+  return 7;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(kCsThreads, 1)
+    masked_sample_cluster_kernel(const ClusterSampleParams p) {
+  using St = typename Elem<DT>::storage;
+  constexpr int kElem = (int)sizeof(St);
+  constexpr int kRb = DT == kBF16 ? 16 : DT == kF16 ? 13 : 0;  // lowest bit a value can set
+  extern __shared__ __align__(16) unsigned char s_dyn[];
+  __shared__ CsMail s_mail[2];
+  __shared__ CsMail s_all[kCsMaxCluster];
+  __shared__ double s_red[kSampleWarps];
+  __shared__ uint32_t s_u[kSampleWarps];
+  __shared__ double s_wmass[kCsWarps];    // per warp: total weight, then kept mass above the cut
+  __shared__ uint32_t s_wcount[kCsWarps];  // per warp: +inf ids, then ties of the cut value
+  __shared__ uint32_t s_bin, s_ties;
+  __shared__ double s_above;
+  __shared__ long long s_take;
+  __shared__ int s_walk_warp;
+  __shared__ double s_walk_before;
+  __shared__ long long s_walk_rank;
+
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int k = p.k;
+  const uint32_t rank = cs_rank();
+  const int64_t row = blockIdx.x / k;
+  const int64_t V = p.vocab;
+  const int64_t lo = (int64_t)rank * p.slice;
+  const int n = (int)max((int64_t)0, min((int64_t)p.slice, V - lo));
+  unsigned char* const s_vals = s_dyn;
+  uint32_t* const s_words = p.mask ? reinterpret_cast<uint32_t*>(s_dyn + p.off_words) : nullptr;
+  WarpBuf* const s_bufs = reinterpret_cast<WarpBuf*>(s_dyn + p.off_work);
+  CsHist* const s_hist = reinterpret_cast<CsHist*>(s_dyn + p.off_work);
+  const int comb_cap = (kCsBins + k - 1) / k;
+  double* const s_comb_p = reinterpret_cast<double*>(s_dyn + p.off_comb);
+  uint32_t* const s_comb_c =
+      reinterpret_cast<uint32_t*>(s_dyn + p.off_comb + ((comb_cap * 8 + 15) & ~15));
+
+  // 0. stage this CTA's ids: values, then mask words
+  {
+    const St* g = static_cast<const St*>(p.logits) + row * p.row_stride + lo;
+    int j = tid;
+    if (((uintptr_t)g & 15u) == 0) {
+      const int nv = (n * kElem) >> 4;
+      const unsigned char* gb = reinterpret_cast<const unsigned char*>(g);
+      for (int q = tid; q < nv; q += kCsThreads) cs_cp_async16(s_vals + 16 * q, gb + 16 * q);
+      j = nv * (16 / kElem) + tid;
+    }
+    for (; j < n; j += kCsThreads) reinterpret_cast<St*>(s_vals)[j] = __ldg(g + j);
+    if (p.mask) {
+      const uint32_t* gm = p.mask + row * p.mask_stride + (lo >> 5);
+      const int nw = (n + 31) >> 5;
+      for (int q = tid; q < nw; q += kCsThreads) cs_cp_async4(s_words + q, gm + q);
+    }
+    cs_cp_async_wait_all();
+    __syncthreads();
+  }
+
+  // warp w owns the contiguous staged ids [wlo, whi)
+  const int wrange = ((n + 31) / 32 + 7) / 8 * 8;
+  const int wlo = min(n, warp * wrange), whi = min(n, wlo + wrange);
+
+  int slot = 0;
+  auto exchange = [&](const CsMail& mine) {
+    if (tid == 0) s_mail[slot] = mine;
+    cs_cluster_sync();
+    if (tid < k) s_all[tid] = *cs_remote(&s_mail[slot], (uint32_t)tid);
+    __syncthreads();
+    slot ^= 1;
+  };
+
+  // 1. support: any valid id, NaN, +inf ids, the largest finite value (as an order code)
+  uint32_t any = 0u, nan = 0u, pinf = 0u, maxo = 0u;
+  for (int s = wlo; s < whi; s += kSampleStep) {
+    float v[8];
+    const uint32_t m = cs_load8<DT>(s_vals, s_words, s + 8 * lane, whi, v);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      if (!((m >> t) & 1u)) continue;
+      any = 1u;
+      const float x = v[t];
+      if (x != x) {
+        nan = 1u;
+      } else if (x == INFINITY) {
+        ++pinf;
+      } else if (x != -INFINITY) {
+        maxo = max(maxo, ord32(x));
+      }
+    }
+  }
+  {
+    const uint32_t wp = __reduce_add_sync(kFull, pinf);
+    if (lane == 0) s_wcount[warp] = wp;
+  }
+  any = block_or_u32(any, s_u);
+  nan = block_or_u32(nan, s_u);
+  pinf = block_sum_u32(pinf, s_u);
+  maxo = block_max_u32(maxo, s_u);
+  {
+    CsMail m = {};
+    m.u[0] = any;
+    m.u[1] = nan;
+    m.u[2] = pinf;
+    m.u[3] = maxo;
+    exchange(m);
+  }
+  uint32_t c_any = 0u, c_nan = 0u, c_pinf = 0u, c_maxo = 0u, pinf_before = 0u;
+  for (int q = 0; q < k; ++q) {
+    c_any |= s_all[q].u[0];
+    c_nan |= s_all[q].u[1];
+    if (q < (int)rank) pinf_before += s_all[q].u[2];
+    c_pinf += s_all[q].u[2];
+    c_maxo = max(c_maxo, s_all[q].u[3]);
+  }
+  const uint32_t status = !c_any ? kStatusEmptyMask
+                          : c_nan ? kStatusNanInSupport
+                          : (!c_pinf && !c_maxo) ? kStatusAllNegInf : 0u;
+  const double u = philox_uniform(p.seed, p.call, (uint32_t)row);
+
+  if (status) {
+    if (rank == 0 && tid == 0) {
+      p.out_idx[row] = -1;
+      p.out_status[row] = status;
+    }
+  } else if (c_pinf) {
+    // 2a. the +inf ids share the mass equally; ranked (equal probabilities) by id
+    if (tid == 0) {
+      const double w = 1.0 / (double)c_pinf;
+      uint32_t m = c_pinf;
+      double cum = 0.0;
+      for (uint32_t j = 1; j <= c_pinf; ++j) {
+        cum += w;
+        if (cum >= p.top_p) {
+          m = j;
+          break;
+        }
+      }
+      double kept_total = 0.0;
+      for (uint32_t j = 0; j < m; ++j) kept_total += w;
+      const double threshold = u * kept_total;
+      uint32_t pick = m - 1;
+      cum = 0.0;
+      for (uint32_t j = 0; j < m; ++j) {
+        cum += w;
+        if (threshold < cum) {
+          pick = j;
+          break;
+        }
+      }
+      s_take = pick;
+      // the warp of this CTA holding the pick, if any
+      s_walk_warp = -1;
+      if (pick >= pinf_before && pick < pinf_before + pinf) {
+        uint32_t before = pinf_before;
+        for (int w2 = 0; w2 < kCsWarps; ++w2) {
+          if (pick < before + s_wcount[w2]) {
+            s_walk_warp = w2;
+            s_walk_rank = (long long)(pick - before);
+            break;
+          }
+          before += s_wcount[w2];
+        }
+      }
+    }
+    __syncthreads();
+    if (warp == s_walk_warp) {
+      uint32_t r = (uint32_t)s_walk_rank;  // the pick among this warp's +inf ids
+      for (int s = wlo; s < whi; s += kSampleStep) {
+        float v[8];
+        const int j0 = s + 8 * lane;
+        const uint32_t m = cs_load8<DT>(s_vals, s_words, j0, whi, v);
+        uint32_t inf_bits = 0u;
+#pragma unroll
+        for (int t = 0; t < 8; ++t)
+          if (((m >> t) & 1u) && v[t] == INFINITY) inf_bits |= 1u << t;
+        const uint32_t c = __popc(inf_bits);
+        uint32_t incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t t = __shfl_up_sync(kFull, incl, o);
+          if (lane >= o) incl += t;
+        }
+        const uint32_t tot = __shfl_sync(kFull, incl, 31);
+        if (r < tot) {
+          if (r >= incl - c && r < incl) {
+            p.out_idx[row] = (int32_t)(lo + j0 + cs_nth_bit8(inf_bits, r - (incl - c)));
+            p.out_status[row] = 0u;
+          }
+          break;
+        }
+        r -= tot;
+      }
+    }
+  } else {
+    // 2b. finite values: weight exp((v - max) / T), zero weights drop out
+    const double vmax = (double)cs_code_to_float(c_maxo);
+    // divide by T, as the reference does: multiplying by 1/T rounds differently
+    auto weight_exact = [&](float x) { return exp(((double)x - vmax) / p.temperature); };
+
+    // 3. total weight and the number of weighted ids
+    double tsum = 0.0;
+    uint32_t nw = 0u;
+    cs_warp_batches<DT>(
+        s_vals, s_words, wlo, whi, &s_bufs[warp],
+        [&](int, const float* v, uint32_t m) {
+          uint32_t keep = 0u;
+#pragma unroll
+          for (int t = 0; t < 8; ++t)
+            if (((m >> t) & 1u) && v[t] != -INFINITY) keep |= 1u << t;
+          return keep;
+        },
+        [&](bool has, int, float x) {
+          if (has) {
+            const double w = weight_exact(x);
+            if (w > 0.0) {
+              tsum += w;
+              ++nw;
+            }
+          }
+          return false;
+        });
+    {
+      const double wt = warp_sum_d(tsum);
+      if (lane == 0) s_wmass[warp] = wt;
+    }
+    nw = block_sum_u32(nw, s_u);  // (its barriers also publish s_wmass)
+    {
+      double ct = 0.0;
+      for (int w2 = 0; w2 < kCsWarps; ++w2) ct += s_wmass[w2];
+      CsMail m = {};
+      m.d[0] = ct;
+      m.u[0] = nw;
+      exchange(m);
+    }
+    double total = 0.0;
+    uint32_t nwt = 0u;
+    for (int q = 0; q < k; ++q) {
+      total += s_all[q].d[0];
+      nwt += s_all[q].u[0];
+    }
+    const bool keep_all = !(p.top_p < 1.0);
+    // candidates: weight >= tau = (1 - top_p) total / (2 n), i.e. value >= vtau; as a float
+    // test, x >= fthr with fthr the least float not below vtau
+    const double tau = (1.0 - p.top_p) * total / (2.0 * (double)nwt);
+    const double vtau = tau > 0.0 ? vmax + p.temperature * log(tau) : -INFINITY;
+    float fthr = (float)vtau;
+    if ((double)fthr < vtau) fthr = nextafterf(fthr, INFINITY);
+
+    // 4. radix levels from below the candidates' common prefix down to one exact value
+    uint32_t vstar = 0u;  // order code of the cut value (0: below every value: keep all)
+    uint32_t ties = 0u;
+    double above = 0.0;  // probability of every id ranked above the current prefix
+    if (!keep_all) {
+      const uint32_t lowc = fthr == -INFINITY ? kOrd32NegInf + 1u : min(ord32(fthr), c_maxo);
+      const uint32_t diff = lowc ^ c_maxo;
+      int top = diff ? 32 - __clz(diff) : 0;  // bits [top, 32) are the same in every candidate
+      if (top < kRb + 1) top = kRb + 1;
+      uint32_t prefix = top >= 32 ? 0u : (c_maxo >> top);
+      int cur = top;
+      while (cur > kRb) {  // cluster-uniform
+        const int width = min(11, cur - kRb);
+        const int shift = cur - width;
+        const int nb = 1 << width;
+        const bool final_level = shift == kRb;
+        for (int b = tid; b < nb; b += kCsThreads) {
+          s_hist->mass[b] = 0.0;
+          s_hist->count[b] = 0u;
+        }
+        __syncthreads();
+        for (int s = wlo; s < whi; s += kSampleStep) {
+          float v[8];
+          const uint32_t m = cs_load8<DT>(s_vals, s_words, s + 8 * lane, whi, v);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            const float x = v[t];
+            if (!((m >> t) & 1u) || !(x >= fthr) || x == -INFINITY) continue;
+            const uint32_t o = ord32(x);
+            if (cur < 32 && (o >> cur) != prefix) continue;
+            const uint32_t b = (o >> shift) & (uint32_t)(nb - 1);
+            if (final_level) {
+              atomicAdd(&s_hist->count[b], 1u);
+            } else {
+              const double w = weight_exact(x);
+              if (w > 0.0) {
+                atomicAdd(&s_hist->mass[b], w);
+                atomicAdd(&s_hist->count[b], 1u);
+              }
+            }
+          }
+        }
+        cs_cluster_sync();  // every CTA's local histogram is complete
+        // this CTA sums its share of the bins over the cluster, in rank order
+        const int per = (nb + k - 1) / k;
+        const int b0 = (int)rank * per, b1 = min(nb, b0 + per);
+        for (int b = b0 + tid; b < b1; b += kCsThreads) {
+          double msum = 0.0;
+          uint32_t csum = 0u;
+          for (int q = 0; q < k; ++q) {
+            const CsHist* h = cs_remote(s_hist, (uint32_t)q);
+            csum += h->count[b];
+            if (!final_level) msum += h->mass[b];
+          }
+          double pb = 0.0;
+          if (final_level) {
+            // one exact value per bin: mass = count x its probability
+            if (csum) {
+              const double w =
+                  weight_exact(cs_code_to_float(cs_full_code<kRb>((prefix << width) | (uint32_t)b)));
+              if (w > 0.0) {
+                pb = (double)csum * (w / total);
+              } else {
+                csum = 0u;
+              }
+            }
+          } else {
+            pb = msum / total;
+          }
+          s_comb_p[b - b0] = pb;
+          s_comb_c[b - b0] = csum;
+        }
+        cs_cluster_sync();  // the combined histogram is complete
+        // thread t owns bins nb-1-2t and nb-2-2t: a scan in descending bin order
+        const int b_hi = nb - 1 - 2 * tid, b_lo = b_hi - 1;
+        double p_hi = 0.0, p_lo = 0.0;
+        uint32_t c_hi = 0u, c_lo = 0u;
+        if (b_hi >= 0) {
+          const int q = b_hi / per, o = b_hi - q * per;
+          p_hi = cs_remote(s_comb_p, (uint32_t)q)[o];
+          c_hi = cs_remote(s_comb_c, (uint32_t)q)[o];
+        }
+        if (b_lo >= 0) {
+          const int q = b_lo / per, o = b_lo - q * per;
+          p_lo = cs_remote(s_comb_p, (uint32_t)q)[o];
+          c_lo = cs_remote(s_comb_c, (uint32_t)q)[o];
+        }
+        double sum_all;
+        const double before = above + block_exclusive_scan_d(p_hi + p_lo, s_red, &sum_all);
+        if (tid == 0) s_bin = 0xFFFFFFFFu;
+        __syncthreads();
+        if (c_hi && before < p.top_p && before + p_hi >= p.top_p) {
+          s_bin = (uint32_t)b_hi;
+          s_above = before;
+          s_ties = c_hi;
+        } else if (c_lo && before + p_hi < p.top_p && before + p_hi + p_lo >= p.top_p) {
+          s_bin = (uint32_t)b_lo;
+          s_above = before + p_hi;
+          s_ties = c_lo;
+        }
+        __syncthreads();
+        if (s_bin == 0xFFFFFFFFu) {
+          // the mass never reaches top_p (rounding): every id of this prefix is kept; go
+          // down into its lowest nonempty bin
+          int mine = -1;
+          if (c_lo) {
+            mine = b_lo;
+          } else if (c_hi) {
+            mine = b_hi;
+          }
+          const uint32_t key = mine >= 0 ? (0x80000000u | (uint32_t)(nb - mine)) : 0u;
+          const uint32_t best = block_max_u32(key, s_u);
+          if (mine >= 0 && (best & 0x7FFFFFFFu) == (uint32_t)(nb - mine)) {
+            s_bin = (uint32_t)mine;
+            s_above = mine == b_lo ? before + p_hi : before;
+            s_ties = mine == b_lo ? c_lo : c_hi;
+          }
+          __syncthreads();
+        }
+        prefix = (prefix << width) | s_bin;
+        above = s_above;
+        ties = s_ties;
+        cur = shift;
+        __syncthreads();
+      }
+      vstar = cs_full_code<kRb>(prefix);
+    }
+    // the ties: ids equal to the cut value, kept in id order while the cumulative sum, added
+    // one by one as the reference does, stays below top_p
+    const double pstar = keep_all ? 0.0 : weight_exact(cs_code_to_float(vstar)) / total;
+    if (tid == 0) {
+      double cum = above;
+      uint32_t take = ties;
+      for (uint32_t j = 1; j <= ties; ++j) {
+        cum += pstar;
+        if (cum >= p.top_p) {
+          take = j;
+          break;
+        }
+      }
+      s_take = take;
+    }
+    __syncthreads();  // (also: every warp is done with the histogram before the buffers)
+    const uint32_t take = (uint32_t)s_take;
+
+    // 5. per warp: probability of the ids ranked above the cut value, and the ties
+    double wabove = 0.0;
+    uint32_t wties = 0u;
+    if (keep_all) {
+      wabove = s_wmass[warp] / total;
+    } else {
+      uint32_t lane_ties = 0u;
+      cs_warp_batches<DT>(
+          s_vals, s_words, wlo, whi, &s_bufs[warp],
+          [&](int, const float* v, uint32_t m) {
+            uint32_t keep = 0u;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              if (!((m >> t) & 1u) || v[t] == -INFINITY) continue;
+              const uint32_t o = ord32(v[t]);
+              if (o > vstar) keep |= 1u << t;
+              if (o == vstar) ++lane_ties;
+            }
+            return keep;
+          },
+          [&](bool has, int, float x) {
+            wabove += warp_sum_d(has ? weight_exact(x) / total : 0.0);
+            return false;
+          });
+      wties = __reduce_add_sync(kFull, lane_ties);
+    }
+    __syncthreads();  // every warp has read s_wmass
+    if (lane == 0) {
+      s_wmass[warp] = wabove;
+      s_wcount[warp] = wties;
+    }
+    __syncthreads();
+    {
+      double ca = 0.0;
+      uint32_t ct = 0u;
+      for (int w2 = 0; w2 < kCsWarps; ++w2) {
+        ca += s_wmass[w2];
+        ct += s_wcount[w2];
+      }
+      CsMail m = {};
+      m.d[0] = ca;
+      m.u[0] = ct;
+      exchange(m);
+    }
+    // kept mass per CTA: above the cut plus its share of the first `take` ties
+    double kept_total = 0.0;
+    {
+      uint32_t tb = 0u;
+      for (int q = 0; q < k; ++q) {
+        const uint32_t tq = s_all[q].u[0];
+        const uint32_t mq = take > tb ? min(take - tb, tq) : 0u;
+        kept_total += s_all[q].d[0] + (double)mq * pstar;
+        tb += tq;
+      }
+    }
+    const double threshold = u * kept_total;
+    // the walk belongs to the last CTA, then the last warp, in id order whose kept mass is
+    // positive and starts at or below the threshold
+    if (tid == 0) {
+      uint32_t tb = 0u;
+      double kb = 0.0;
+      int chosen = -1;
+      double chosen_before = 0.0;
+      uint32_t chosen_ties = 0u;
+      for (int q = 0; q < k; ++q) {
+        const uint32_t tq = s_all[q].u[0];
+        const uint32_t mq = take > tb ? min(take - tb, tq) : 0u;
+        const double kq = s_all[q].d[0] + (double)mq * pstar;
+        if (kq > 0.0 && kb <= threshold) {
+          chosen = q;
+          chosen_before = kb;
+          chosen_ties = tb;
+        }
+        kb += kq;
+        tb += tq;
+      }
+      s_walk_warp = -1;
+      if (chosen == (int)rank) {
+        tb = chosen_ties;
+        kb = chosen_before;
+        for (int w2 = 0; w2 < kCsWarps; ++w2) {
+          const uint32_t tw = s_wcount[w2];
+          const uint32_t mw = take > tb ? min(take - tb, tw) : 0u;
+          const double kw = s_wmass[w2] + (double)mw * pstar;
+          if (kw > 0.0 && kb <= threshold) {
+            s_walk_warp = w2;
+            s_walk_before = kb;
+            s_walk_rank = tb;
+          }
+          kb += kw;
+          tb += tw;
+        }
+      }
+    }
+    __syncthreads();
+    if (warp == s_walk_warp) {
+      // 6. the draw: walk this warp's kept ids in id order with running sums
+      double cum = s_walk_before;
+      uint32_t tie_rank = (uint32_t)s_walk_rank;  // ties of the cut value before this step
+      int pick = -1, last = -1;  // slice-relative
+      cs_warp_batches<DT>(
+          s_vals, s_words, wlo, whi, &s_bufs[warp],
+          [&](int, const float* v, uint32_t m) {
+            uint32_t above_bits = 0u, tie_bits = 0u;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              if (!((m >> t) & 1u) || v[t] == -INFINITY) continue;
+              const uint32_t o = ord32(v[t]);
+              if (o > vstar) above_bits |= 1u << t;
+              if (o == vstar && !keep_all) tie_bits |= 1u << t;
+            }
+            // ranks of this lane's ties among the row's ties, in id order
+            const uint32_t c = __popc(tie_bits);
+            uint32_t incl = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const uint32_t t = __shfl_up_sync(kFull, incl, o);
+              if (lane >= o) incl += t;
+            }
+            uint32_t r = tie_rank + incl - c;
+            tie_rank += __shfl_sync(kFull, incl, 31);
+            uint32_t keep = above_bits;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              if ((tie_bits >> t) & 1u) {
+                if (r < take) keep |= 1u << t;
+                ++r;
+              }
+            }
+            return keep;
+          },
+          [&](bool has, int j, float x) {
+            const double pi = has ? weight_exact(x) / total : 0.0;
+            double run = pi;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const double t = __shfl_up_sync(kFull, run, o);
+              if (lane >= o) run += t;
+            }
+            const unsigned hit = __ballot_sync(kFull, has && pi > 0.0 && threshold < cum + run);
+            const int lastj = __reduce_max_sync(kFull, (has && pi > 0.0) ? (uint32_t)(j + 1) : 0u);
+            if (lastj) last = lastj - 1;
+            if (hit) {
+              pick = __shfl_sync(kFull, j, __ffs(hit) - 1);
+              return true;
+            }
+            cum += __shfl_sync(kFull, run, 31);
+            return false;
+          });
+      if (pick < 0) pick = last;  // the draw lies past this warp's sum (rounding)
+      if (lane == 0) {
+        p.out_idx[row] = (int32_t)(lo + pick);
+        p.out_status[row] = 0u;
+      }
+    }
+  }
+  cs_cluster_sync();  // no CTA leaves while another may still read its shared memory
+}

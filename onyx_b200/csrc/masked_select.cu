@@ -1090,6 +1090,7 @@ __global__ void combine_keys_kernel(const unsigned long long* keys, int64_t n_pa
 #include "peer_exchange.cuh"
 #include "dfa_masks.cuh"
 #include "masked_sample.cuh"
+#include "masked_sample_cluster.cuh"
 
 // ---------------------------------------------------------------------------------------
 // host side
@@ -1508,6 +1509,173 @@ int onyx_vocab_partial_argmax(const void* logits, int dtype, int64_t rows, int64
   return finish_launch(dispatch<kModeKey>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled()));
 }
 
+// ---- masked sampling: cluster form ------------------------------------------------------
+
+// ONYX_B200_SAMPLE_FORM (a diagnostic and test switch, read at every call): "single" runs
+// the one-CTA-per-row kernel for every shape; "cluster:<k>" asks for k CTAs per row (raised
+// to the least k whose shared memory holds a row). Unset: the cluster form with k chosen
+// from the batch size, wherever a row fits.
+static int sample_form() {
+  const char* v = getenv("ONYX_B200_SAMPLE_FORM");
+  if (!v) return 0;
+  if (strcmp(v, "single") == 0) return -1;
+  if (strncmp(v, "cluster:", 8) == 0) {
+    const int k = atoi(v + 8);
+    if (k >= 1 && k <= kCsMaxCluster) return k;
+  }
+  return 0;
+}
+
+constexpr int kNoClusterPlan = -1000;
+
+struct ClusterSamplePlan {
+  int k = 0, slice = 0, off_words = 0, off_work = 0, off_comb = 0;
+  size_t smem = 0;
+};
+
+static size_t cs_align16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+// shared memory of the cluster form with k CTAs per row (0: it cannot fit)
+static ClusterSamplePlan cs_layout(int k, int64_t vocab, int elem, bool masked) {
+  ClusterSamplePlan pl;
+  const int64_t per = (vocab + k - 1) / k;
+  const int64_t slice = (per + kCsSliceAlign - 1) / kCsSliceAlign * kCsSliceAlign;
+  if (slice > (1 << 26)) return pl;
+  pl.k = k;
+  pl.slice = (int)slice;
+  size_t off = cs_align16((size_t)slice * elem);
+  pl.off_words = (int)off;
+  if (masked) off += cs_align16((size_t)slice / 32 * 4);
+  pl.off_work = (int)off;
+  off += sizeof(WarpBuf) * kCsWarps;
+  pl.off_comb = (int)off;
+  const size_t cap = (kCsBins + k - 1) / k;
+  off += cs_align16(cap * 8) + cs_align16(cap * 4);
+  pl.smem = off;
+  return pl;
+}
+static_assert(sizeof(WarpBuf) * kCsWarps >= sizeof(CsHist), "histogram overlays the buffers");
+
+static const void* cs_kernel(int dtype) {
+  return dtype == kBF16 ? (const void*)masked_sample_cluster_kernel<kBF16>
+         : dtype == kF16 ? (const void*)masked_sample_cluster_kernel<kF16>
+                         : (const void*)masked_sample_cluster_kernel<kF32>;
+}
+
+// Launches the cluster form, or returns kNoClusterPlan when no cluster of at most 16 CTAs
+// holds a row in shared memory (the caller then runs the one-CTA kernel).
+static int launch_cluster_sample(int dtype, const SampleParams& sp, int dev, cudaStream_t stream,
+                                 int forced_k) {
+  struct DevInfo {
+    bool ready = false;
+    int sms = 0, max_dyn = 0;
+    int fits[3][kCsMaxCluster + 1];  // per dtype and k: -1 unknown, 0 no, 1 yes (occupancy)
+  };
+  static std::mutex mu;
+  static DevInfo info[64];
+  const int di = dtype == kBF16 ? 0 : dtype == kF16 ? 1 : 2;
+  const void* fn = cs_kernel(dtype);
+  std::lock_guard<std::mutex> lock(mu);
+  DevInfo& d = info[dev];
+  if (!d.ready) {
+    int optin = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+      e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return finish_launch(e);
+    cudaFuncAttributes fa = {};
+    e = cudaFuncGetAttributes(&fa, cs_kernel(kBF16));
+    if (e != cudaSuccess) return finish_launch(e);
+    d.max_dyn = optin - (int)fa.sharedSizeBytes - 1024;  // margin for the other instantiations
+    for (const void* f : {cs_kernel(kBF16), cs_kernel(kF16), cs_kernel(kF32)}) {
+      e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_dyn);
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e != cudaSuccess) return finish_launch(e);
+    }
+    for (auto& r : d.fits)
+      for (int& x : r) x = -1;
+    d.ready = true;
+  }
+  const int elem = dtype == kF32 ? 4 : 2;
+  const bool masked = sp.mask != nullptr;
+  int k_fit = 0;
+  for (int k = 1; k <= kCsMaxCluster; ++k) {
+    const ClusterSamplePlan pl = cs_layout(k, sp.vocab, elem, masked);
+    if (pl.k && pl.smem <= (size_t)d.max_dyn) {
+      k_fit = k;
+      break;
+    }
+  }
+  if (!k_fit) return kNoClusterPlan;
+  // spread small batches over the SMs, at least 4096 ids per CTA
+  int64_t k_par = d.sms / std::max<int64_t>(1, sp.rows);
+  k_par = std::min<int64_t>(k_par, (sp.vocab + 4095) / 4096);
+  if (forced_k) k_par = forced_k;
+  int k = (int)std::max<int64_t>(k_fit, std::min<int64_t>(k_par, kCsMaxCluster));
+  if ((int64_t)k * sp.rows > 0x7FFFFFFFll) return kNoClusterPlan;
+  for (;; --k) {
+    if (k < k_fit) return kNoClusterPlan;
+    const ClusterSamplePlan pl = cs_layout(k, sp.vocab, elem, masked);
+    int& fits = d.fits[di][k];
+    if (fits < 0) {
+      cudaLaunchConfig_t q = {};
+      cudaLaunchAttribute qa[1];
+      qa[0].id = cudaLaunchAttributeClusterDimension;
+      qa[0].val.clusterDim.x = (unsigned)k;
+      qa[0].val.clusterDim.y = 1;
+      qa[0].val.clusterDim.z = 1;
+      q.gridDim = dim3((unsigned)k, 1, 1);
+      q.blockDim = dim3(kCsThreads, 1, 1);
+      q.dynamicSmemBytes = (size_t)d.max_dyn;  // the largest layout: a bound for every shape
+      q.attrs = qa;
+      q.numAttrs = 1;
+      int clusters = 0;
+      const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, fn, &q);
+      if (e != cudaSuccess) (void)cudaGetLastError();
+      fits = (e == cudaSuccess && clusters > 0) ? 1 : 0;
+    }
+    if (!fits) continue;
+    ClusterSampleParams cp = {};
+    cp.logits = sp.logits;
+    cp.row_stride = sp.row_stride;
+    cp.vocab = sp.vocab;
+    cp.mask = sp.mask;
+    cp.mask_stride = sp.mask_stride;
+    cp.temperature = sp.temperature;
+    cp.top_p = sp.top_p;
+    cp.seed = sp.seed;
+    cp.call = sp.call;
+    cp.out_idx = sp.out_idx;
+    cp.out_status = sp.out_status;
+    cp.k = k;
+    cp.slice = pl.slice;
+    cp.off_words = pl.off_words;
+    cp.off_work = pl.off_work;
+    cp.off_comb = pl.off_comb;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)k;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(k * sp.rows), 1, 1);
+    cfg.blockDim = dim3(kCsThreads, 1, 1);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    cudaError_t e;
+    switch (dtype) {
+      case kBF16: e = cudaLaunchKernelEx(&cfg, masked_sample_cluster_kernel<kBF16>, cp); break;
+      case kF16: e = cudaLaunchKernelEx(&cfg, masked_sample_cluster_kernel<kF16>, cp); break;
+      default: e = cudaLaunchKernelEx(&cfg, masked_sample_cluster_kernel<kF32>, cp); break;
+    }
+    return finish_launch(e);
+  }
+}
+
 int onyx_masked_sample(const void* logits, int dtype, int64_t rows, int64_t vocab,
                        int64_t row_stride, const uint32_t* mask, int64_t mask_stride,
                        double temperature, double top_p, uint64_t seed, uint64_t call,
@@ -1534,6 +1702,15 @@ int onyx_masked_sample(const void* logits, int dtype, int64_t rows, int64_t voca
   sp.rows = rows;
   sp.out_idx = out_idx;
   sp.out_status = out_status;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return finish_launch(e);
+  if (dev < 0 || dev >= 64) return ONYX_ERR_INVALID_ARGUMENT;
+  const int form = sample_form();
+  if (form >= 0) {
+    const int rc = launch_cluster_sample(dtype, sp, dev, (cudaStream_t)stream, form);
+    if (rc != kNoClusterPlan) return rc;
+  }
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -1545,14 +1722,10 @@ int onyx_masked_sample(const void* logits, int dtype, int64_t rows, int64_t voca
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
   cfg.dynamicSmemBytes = kSampleSmemBytes;
   // the compaction buffers take 48 KB of dynamic shared memory: opt in once per device
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return finish_launch(e);
   {
     static std::mutex mu;
     static bool ready[64] = {};
     std::lock_guard<std::mutex> lock(mu);
-    if (dev < 0 || dev >= 64) return ONYX_ERR_INVALID_ARGUMENT;
     if (!ready[dev]) {
       for (const void* fn : {(const void*)masked_sample_kernel<kBF16>,
                              (const void*)masked_sample_kernel<kF16>,

@@ -21,6 +21,19 @@ from tests.gpu_util import host, masks_to_device, requires_cuda, to_device
 
 pytestmark = [pytest.mark.gpu, requires_cuda]
 
+# Kernel forms: the default (a cluster of CTAs per row, sized from the batch), the one-CTA
+# kernel, and clusters of 3 and 16 CTAs (ONYX_B200_SAMPLE_FORM, read at every call).
+FORMS = ["default", "single", "cluster:3", "cluster:16"]
+
+
+@pytest.fixture(params=FORMS)
+def form(request, monkeypatch):
+    if request.param == "default":
+        monkeypatch.delenv("ONYX_B200_SAMPLE_FORM", raising=False)
+    else:
+        monkeypatch.setenv("ONYX_B200_SAMPLE_FORM", request.param)
+    return request.param
+
 
 def _float64(x: np.ndarray, dtype: str) -> np.ndarray:
     if dtype == "bf16":
@@ -39,7 +52,7 @@ def _check(x, m, dtype, temperature, top_p, seed, call):
 
 @pytest.mark.parametrize("dtype", ["bf16", "f16", "f32"])
 @pytest.mark.parametrize("policy", [(1.0, 1.0), (0.8, 0.9), (0.5, 0.3), (2.0, 0.99), (1.0, 0.02)])
-def test_random_rows_match_oracle(dtype, policy, cuda_lib):
+def test_random_rows_match_oracle(dtype, policy, form, cuda_lib):
     rng = np.random.default_rng(len(dtype) * 100 + int(policy[1] * 1000))
     vocab = 5003
     rows = 12
@@ -53,7 +66,7 @@ def test_random_rows_match_oracle(dtype, policy, cuda_lib):
         _check(x, m, dtype, policy[0], policy[1], 1234, call)
 
 
-def test_full_vocabulary_rows(cuda_lib):
+def test_full_vocabulary_rows(form, cuda_lib):
     w = workloads.batched(rows=8)
     for seed, (t, tp) in ((5, (0.8, 0.9)), (6, (1.0, 1.0)), (7, (0.3, 0.5))):
         _check(w["logits_bf16"], w["masks"], "bf16", t, tp, seed, 3)
@@ -61,7 +74,7 @@ def test_full_vocabulary_rows(cuda_lib):
     _check(w["logits_bf16"], None, "bf16", 1.0, 0.95, 11, 0)
 
 
-def test_special_rows(cuda_lib):
+def test_special_rows(form, cuda_lib):
     vocab = 300
     x = np.zeros((8, vocab), np.float32)
     rng = np.random.default_rng(3)
@@ -83,6 +96,52 @@ def test_special_rows(cuda_lib):
     st = host(sampling.masked_sample(to_device(x, "f32"), masks_to_device(m), temperature=1.0,
                                      top_p=1.0, seed=1).status)
     assert list(st[2:5]) == [ms.STATUS_NAN_IN_SUPPORT, ms.STATUS_ALL_NEG_INF, ms.STATUS_EMPTY_MASK]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16", "f32"])
+def test_wide_value_ranges(dtype, form, cuda_lib):
+    """Candidates on both sides of zero and over many exponents (a hot temperature or a
+    top_p near 1): the radix select starts at the sign bit and takes several levels."""
+    rng = np.random.default_rng(77)
+    rows, vocab = 6, 9001
+    x = rng.standard_normal((rows, vocab)) * np.array([[0.3], [3.0], [30.0], [1.0], [8.0], [0.01]])
+    x = x.astype(np.float32)
+    if dtype == "bf16":
+        x = workloads.bf16_bits(x)
+    elif dtype == "f16":
+        x = x.astype(np.float16)
+    m = workloads.bernoulli_masks(rng, rng.uniform(0.05, 1.0, rows), vocab)
+    for t, tp in ((50.0, 0.9), (5.0, 0.999), (1.0, 0.5), (0.05, 0.95)):
+        for call in (0, 3):
+            _check(x, m, dtype, t, tp, 4242, call)
+
+
+def test_unaligned_rows(form, cuda_lib):
+    """Rows whose start is not 16-byte aligned (a column slice) stage element by element."""
+    rng = np.random.default_rng(5)
+    full = workloads.normal_bf16(rng, (4, 3001))
+    xt = to_device(full, "bf16")[:, 1:]
+    x = full[:, 1:]
+    m = workloads.bernoulli_masks(rng, np.array([0.5, 0.1, 1.0, 0.02]), 3000)
+    for call in range(3):
+        r = sampling.masked_sample(xt, masks_to_device(m), temperature=0.9, top_p=0.8,
+                                   seed=8, call=call)
+        idx_ref, st_ref = osamp.masked_sample(_float64(x, "bf16"), m, 0.9, 0.8, 8, call)
+        np.testing.assert_array_equal(host(r.status).astype(np.uint32), st_ref)
+        np.testing.assert_array_equal(host(r.token_ids), idx_ref)
+
+
+def test_many_ties_at_the_cut(form, cuda_lib):
+    """Hundreds of ids share the value the cut falls on; the kept ones are the first in id
+    order, spread over several warps and CTAs."""
+    vocab = 20000
+    x = np.full((3, vocab), -5.0, np.float32)
+    x[:, ::7] = 1.0     # 2858 ties at the top
+    x[1, 100] = 2.0     # one id above them
+    x[2, ::5000] = 3.0  # four ids above them
+    for tp in (0.1, 0.5, 0.97):
+        for call in range(4):
+            _check(x, None, "f32", 1.0, tp, 31, call)
 
 
 @pytest.mark.parametrize("case", load_golden("sampling_cases.json")["cases"][:18],
