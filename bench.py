@@ -7,7 +7,8 @@ launch over one 64-row batch. Sixteen distinct input sets (279 MB, more than twi
 replayed from CUDA graphs.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload batched|spec_verify|table_gather|scaling|vocab_parallel]
+                    [--workload batched|spec_verify|table_gather|scaling|vocab_parallel|
+                                dfa_masks|sample]
 
 One process per GPU (torchrun for N > 1). Batches shard over ranks with no communication
 ("weak" scaling) except ``vocab_parallel``, which splits the vocabulary and all-gathers
@@ -58,6 +59,9 @@ WORKLOADS = {
                     desc="batch-sharded masked argmax bf16 [128/GPU,256000] at 5% density"),
     "vocab_parallel": dict(rows=1024, vocab=256000,
                            desc="vocabulary-sharded masked argmax bf16 [1024,256000/N] + NCCL all-gather"),
+    "sample": dict(rows=64, vocab=128256, temperature=0.8, top_p=0.9,
+                   desc="masked temperature / top-p sampling bf16 [64,128256], mask u32 [64,4008], "
+                        "T=0.8, top_p=0.9"),
     "dfa_masks": dict(rows=64, vocab=128256,
                       desc="mask producer: valid-token masks of every state of a 64-state DFA "
                            "over 128,256 tokens, u32 [64,4008]"),
@@ -175,7 +179,7 @@ class ClockSampler:
 def _cpu_inputs(name: str):
     from onyx_b200 import workloads
 
-    if name in ("batched",):
+    if name in ("batched", "sample"):
         w = workloads.batched()
         return w
     if name == "table_gather":
@@ -209,6 +213,21 @@ def cpu_measure(name: str, budget_s: float, steps: int | None = None, warmup: in
 
         rows_per_call = w["logits_bf16"].shape[0]
         what = "spec verify of 32 entries x 5 rows x 151936 bf16"
+    elif name == "sample":
+        from oracle import sampling as osamp
+        from onyx_b200 import workloads
+
+        w = _cpu_inputs(name)
+        spec = WORKLOADS[name]
+        xs = workloads.bf16_bits_to_f32(w["logits_bf16"][:2]).astype(np.float64)
+        ms_ = w["masks"][:2]
+        threads = 1  # the float64 oracle is plain Python
+
+        def run_once():
+            osamp.masked_sample(xs, ms_, spec["temperature"], spec["top_p"], 1234, 0)
+
+        rows_per_call = 2
+        what = "masked sampling of 2 rows x 128256 bf16 (the float64 oracle, one thread)"
     elif name == "dfa_masks":
         w = _cpu_inputs(name)
 
@@ -289,7 +308,7 @@ def run_ours(args) -> None:
     import torch.distributed as dist
 
     from onyx_b200 import masked_selection as ms
-    from onyx_b200 import vocab_parallel, workloads
+    from onyx_b200 import sampling, vocab_parallel, workloads
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -322,7 +341,7 @@ def run_ours(args) -> None:
     # ---- inputs, one seeded set copied into R rotating device buffers -------------------
     seed_shift = 17 * rank
     exchange = None  # vocab_parallel over NVLink peer memory (collective set-up)
-    if name == "batched":
+    if name in ("batched", "sample"):
         w = workloads.batched(seed=workloads.SEEDS[2] + seed_shift)
         host_in = {"x": w["logits_bf16"], "m": w["masks"]}
     elif name == "table_gather":
@@ -369,6 +388,9 @@ def run_ours(args) -> None:
             return ms.masked_argmax(b["x"], b["m"])
         if name == "table_gather":
             return ms.gather_masked_argmax(b["x"], table, b["ids"])
+        if name == "sample":
+            return sampling.masked_sample(b["x"], b["m"], temperature=spec["temperature"],
+                                          top_p=spec["top_p"], seed=1234 + rank, call=k)
         if name == "spec_verify":
             return ms.spec_verify(b["x"], b["m"], b["d"])
         if name == "vocab_parallel":
@@ -489,6 +511,10 @@ def run_ours(args) -> None:
             out = (r.token_ids, r.status)
         elif name == "table_gather":
             r = ms.gather_masked_argmax(xin, table, dev_in["ids"])
+            out = (r.token_ids, r.status)
+        elif name == "sample":
+            r = sampling.masked_sample(xin, dev_in["m"], temperature=spec["temperature"],
+                                       top_p=spec["top_p"], seed=1234 + rank, call=0)
             out = (r.token_ids, r.status)
         elif name == "spec_verify":
             r = ms.spec_verify(xin, dev_in["m"], dev_in["d"])

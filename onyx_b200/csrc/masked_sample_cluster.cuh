@@ -83,7 +83,7 @@ __device__ __forceinline__ uint32_t cs_rank() {
 template <class T>
 __device__ __forceinline__ const T* cs_remote(const T* p, uint32_t rank) {
   unsigned long long out;
-  asm volatile("mapa.u64 %0, %1, %2;" : "=l"(out) : "l"(p), "r"(rank));
+  asm("mapa.u64 %0, %1, %2;" : "=l"(out) : "l"(p), "r"(rank));
   return reinterpret_cast<const T*>(out);
 }
 
@@ -159,6 +159,7 @@ __device__ __forceinline__ void cs_warp_batches(const unsigned char* vals, const
     float v[8];
     const uint32_t m = cs_load8<DT>(vals, words, j0, hi, v);
     const uint32_t keep = keep8(j0, v, m);
+    if (!__any_sync(kFull, keep != 0u)) continue;  // nothing kept in this step
     const uint32_t cnt = __popc(keep);
     uint32_t incl = cnt;
 #pragma unroll
@@ -285,52 +286,55 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     slot ^= 1;
   };
 
-  // 1. support: any valid id, NaN, +inf ids, the largest finite value (as an order code)
-  uint32_t any = 0u, nan = 0u, pinf = 0u, maxo = 0u;
-  for (int s = wlo; s < whi; s += kSampleStep) {
-    float v[8];
-    const uint32_t m = cs_load8<DT>(s_vals, s_words, s + 8 * lane, whi, v);
-#pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      if (!((m >> t) & 1u)) continue;
-      any = 1u;
-      const float x = v[t];
-      if (x != x) {
-        nan = 1u;
-      } else if (x == INFINITY) {
-        ++pinf;
-      } else if (x != -INFINITY) {
-        maxo = max(maxo, ord32(x));
+  // 1. support: the masked, NaN-propagating maximum (packed pairs for 16-bit types); any
+  //    valid id at all
+  uint32_t any = 0u, lcode;
+  {
+    float lmax = -INFINITY;
+    uint32_t pm = 0u;
+    if constexpr (DT != kF32) pm = Packed16<DT>::kNegInfPair;
+    for (int s = wlo; s < whi; s += kSampleStep) {
+      const int j0 = s + 8 * lane;
+      if (j0 >= whi) continue;
+      uint32_t m = s_words ? (s_words[j0 >> 5] >> (j0 & 31)) & 0xFFu : 0xFFu;
+      const int left = whi - j0;
+      if (left < 8) m &= (1u << left) - 1u;
+      any |= m;
+      if constexpr (DT == kF32) {
+        const uint4 a = *reinterpret_cast<const uint4*>(s_vals + (size_t)j0 * 4);
+        const uint4 b = *reinterpret_cast<const uint4*>(s_vals + (size_t)j0 * 4 + 16);
+        lmax = max_nan_f32(lmax, max_nan_f32(Vec16<kF32>::masked_max(a, m & 0xFu),
+                                             Vec16<kF32>::masked_max(b, m >> 4)));
+      } else {
+        const uint4 a = *reinterpret_cast<const uint4*>(s_vals + (size_t)j0 * 2);
+        pm = Packed16<DT>::pmax(pm, Packed16<DT>::masked_pair_max(a, m));
       }
     }
+    if constexpr (DT != kF32) lmax = Packed16<DT>::pair_to_f32_max(pm);
+    lcode = ord32(lmax);  // NaN: the largest code
   }
   {
-    const uint32_t wp = __reduce_add_sync(kFull, pinf);
-    if (lane == 0) s_wcount[warp] = wp;
-  }
-  any = block_or_u32(any, s_u);
-  nan = block_or_u32(nan, s_u);
-  pinf = block_sum_u32(pinf, s_u);
-  maxo = block_max_u32(maxo, s_u);
-  {
+    const uint32_t wa = __reduce_or_sync(kFull, any), wc = __reduce_max_sync(kFull, lcode);
+    if (lane == 0) {
+      s_wcount[warp] = wa;
+      s_u[warp] = wc;
+    }
+    __syncthreads();
     CsMail m = {};
-    m.u[0] = any;
-    m.u[1] = nan;
-    m.u[2] = pinf;
-    m.u[3] = maxo;
-    exchange(m);
+    m.u[0] = __reduce_or_sync(kFull, s_wcount[lane]);
+    m.u[1] = __reduce_max_sync(kFull, s_u[lane]);
+    exchange(m);  // (its barriers also end every read of s_wcount and s_u)
   }
-  uint32_t c_any = 0u, c_nan = 0u, c_pinf = 0u, c_maxo = 0u, pinf_before = 0u;
+  uint32_t c_any = 0u, c_code = 0u;
   for (int q = 0; q < k; ++q) {
     c_any |= s_all[q].u[0];
-    c_nan |= s_all[q].u[1];
-    if (q < (int)rank) pinf_before += s_all[q].u[2];
-    c_pinf += s_all[q].u[2];
-    c_maxo = max(c_maxo, s_all[q].u[3]);
+    c_code = max(c_code, s_all[q].u[1]);
   }
+  constexpr uint32_t kOrd32PosInf = 0xFF800000u;
   const uint32_t status = !c_any ? kStatusEmptyMask
-                          : c_nan ? kStatusNanInSupport
-                          : (!c_pinf && !c_maxo) ? kStatusAllNegInf : 0u;
+                          : c_code == kOrd32NaN ? kStatusNanInSupport
+                          : c_code == kOrd32NegInf ? kStatusAllNegInf : 0u;
+  const uint32_t c_maxo = c_code;  // the largest finite value when status == 0 and no +inf
   const double u = philox_uniform(p.seed, p.call, (uint32_t)row);
 
   if (status) {
@@ -338,8 +342,32 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       p.out_idx[row] = -1;
       p.out_status[row] = status;
     }
-  } else if (c_pinf) {
-    // 2a. the +inf ids share the mass equally; ranked (equal probabilities) by id
+  } else if (c_code == kOrd32PosInf) {
+    // 2a. the +inf ids share the mass equally; ranked (equal probabilities) by id. Count
+    //     them per warp and per CTA.
+    uint32_t pinf = 0u;
+    for (int s = wlo; s < whi; s += kSampleStep) {
+      float v[8];
+      const uint32_t m = cs_load8<DT>(s_vals, s_words, s + 8 * lane, whi, v);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) pinf += (((m >> t) & 1u) && v[t] == INFINITY) ? 1u : 0u;
+    }
+    {
+      const uint32_t wp = __reduce_add_sync(kFull, pinf);
+      if (lane == 0) s_wcount[warp] = wp;
+    }
+    __syncthreads();
+    pinf = __reduce_add_sync(kFull, s_wcount[lane]);
+    {
+      CsMail m = {};
+      m.u[0] = pinf;
+      exchange(m);
+    }
+    uint32_t c_pinf = 0u, pinf_before = 0u;
+    for (int q = 0; q < k; ++q) {
+      if (q < (int)rank) pinf_before += s_all[q].u[0];
+      c_pinf += s_all[q].u[0];
+    }
     if (tid == 0) {
       const double w = 1.0 / (double)c_pinf;
       uint32_t m = c_pinf;
@@ -437,15 +465,19 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         });
     {
       const double wt = warp_sum_d(tsum);
-      if (lane == 0) s_wmass[warp] = wt;
+      const uint32_t wn = __reduce_add_sync(kFull, nw);
+      if (lane == 0) {
+        s_wmass[warp] = wt;
+        s_wcount[warp] = wn;
+      }
     }
-    nw = block_sum_u32(nw, s_u);  // (its barriers also publish s_wmass)
+    __syncthreads();
     {
       double ct = 0.0;
       for (int w2 = 0; w2 < kCsWarps; ++w2) ct += s_wmass[w2];
       CsMail m = {};
       m.d[0] = ct;
-      m.u[0] = nw;
+      m.u[0] = __reduce_add_sync(kFull, s_wcount[lane]);
       exchange(m);
     }
     double total = 0.0;
@@ -509,12 +541,22 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         const int per = (nb + k - 1) / k;
         const int b0 = (int)rank * per, b1 = min(nb, b0 + per);
         for (int b = b0 + tid; b < b1; b += kCsThreads) {
-          double msum = 0.0;
+          // every remote read in flight at once, then the sums in rank order
+          uint32_t cq[kCsMaxCluster];
+#pragma unroll
+          for (int q = 0; q < kCsMaxCluster; ++q)
+            cq[q] = q < k ? cs_remote(s_hist, (uint32_t)q)->count[b] : 0u;
           uint32_t csum = 0u;
-          for (int q = 0; q < k; ++q) {
-            const CsHist* h = cs_remote(s_hist, (uint32_t)q);
-            csum += h->count[b];
-            if (!final_level) msum += h->mass[b];
+#pragma unroll
+          for (int q = 0; q < kCsMaxCluster; ++q) csum += cq[q];
+          double msum = 0.0;
+          if (!final_level) {
+            double mq[kCsMaxCluster];
+#pragma unroll
+            for (int q = 0; q < kCsMaxCluster; ++q)
+              mq[q] = q < k ? cs_remote(s_hist, (uint32_t)q)->mass[b] : 0.0;
+#pragma unroll
+            for (int q = 0; q < kCsMaxCluster; ++q) msum += mq[q];
           }
           double pb = 0.0;
           if (final_level) {
@@ -591,7 +633,10 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     }
     // the ties: ids equal to the cut value, kept in id order while the cumulative sum, added
     // one by one as the reference does, stays below top_p
-    const double pstar = keep_all ? 0.0 : weight_exact(cs_code_to_float(vstar)) / total;
+    // as a float: ord32 order is float order with -0 == +0, and no value here is NaN; with
+    // every weighted id kept, -inf is the bound (above it: every finite value)
+    const float vstar_f = keep_all ? -INFINITY : cs_code_to_float(vstar);
+    const double pstar = keep_all ? 0.0 : weight_exact(vstar_f) / total;
     if (tid == 0) {
       double cum = above;
       uint32_t take = ties;
@@ -620,10 +665,9 @@ __global__ void __launch_bounds__(kCsThreads, 1)
             uint32_t keep = 0u;
 #pragma unroll
             for (int t = 0; t < 8; ++t) {
-              if (!((m >> t) & 1u) || v[t] == -INFINITY) continue;
-              const uint32_t o = ord32(v[t]);
-              if (o > vstar) keep |= 1u << t;
-              if (o == vstar) ++lane_ties;
+              if (!((m >> t) & 1u)) continue;
+              if (v[t] > vstar_f) keep |= 1u << t;
+              if (v[t] == vstar_f) ++lane_ties;
             }
             return keep;
           },
@@ -664,41 +708,57 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     }
     const double threshold = u * kept_total;
     // the walk belongs to the last CTA, then the last warp, in id order whose kept mass is
-    // positive and starts at or below the threshold
-    if (tid == 0) {
-      uint32_t tb = 0u;
-      double kb = 0.0;
-      int chosen = -1;
-      double chosen_before = 0.0;
-      uint32_t chosen_ties = 0u;
-      for (int q = 0; q < k; ++q) {
-        const uint32_t tq = s_all[q].u[0];
-        const uint32_t mq = take > tb ? min(take - tb, tq) : 0u;
-        const double kq = s_all[q].d[0] + (double)mq * pstar;
-        if (kq > 0.0 && kb <= threshold) {
-          chosen = q;
-          chosen_before = kb;
-          chosen_ties = tb;
+    // positive and starts at or below the threshold (warp 0 scans: lane q holds CTA q, then
+    // lane w holds warp w)
+    if (warp == 0) {
+      auto excl_u = [&](uint32_t x) {
+        uint32_t incl = x;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t t = __shfl_up_sync(kFull, incl, o);
+          if (lane >= o) incl += t;
         }
-        kb += kq;
-        tb += tq;
-      }
-      s_walk_warp = -1;
+        return incl - x;
+      };
+      auto excl_d = [&](double x) {
+        double incl = x;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const double t = __shfl_up_sync(kFull, incl, o);
+          if (lane >= o) incl += t;
+        }
+        const double e = __shfl_up_sync(kFull, incl, 1);
+        return lane == 0 ? 0.0 : e;
+      };
+      const uint32_t tq = lane < k ? s_all[lane].u[0] : 0u;
+      const uint32_t tbq = excl_u(tq);
+      const uint32_t mq = take > tbq ? min(take - tbq, tq) : 0u;
+      const double kq = lane < k ? s_all[lane].d[0] + (double)mq * pstar : 0.0;
+      const double kbq = excl_d(kq);
+      const unsigned cq = __ballot_sync(kFull, kq > 0.0 && kbq <= threshold);
+      const int chosen = cq ? 31 - __clz(cq) : -1;
+      int walk = -1;
+      double walk_before = 0.0;
+      uint32_t walk_rank = 0u;
       if (chosen == (int)rank) {
-        tb = chosen_ties;
-        kb = chosen_before;
-        for (int w2 = 0; w2 < kCsWarps; ++w2) {
-          const uint32_t tw = s_wcount[w2];
-          const uint32_t mw = take > tb ? min(take - tb, tw) : 0u;
-          const double kw = s_wmass[w2] + (double)mw * pstar;
-          if (kw > 0.0 && kb <= threshold) {
-            s_walk_warp = w2;
-            s_walk_before = kb;
-            s_walk_rank = tb;
-          }
-          kb += kw;
-          tb += tw;
+        const double cbefore = __shfl_sync(kFull, kbq, chosen);
+        const uint32_t cties = __shfl_sync(kFull, tbq, chosen);
+        const uint32_t tw = s_wcount[lane];
+        const uint32_t tbw = cties + excl_u(tw);
+        const uint32_t mw = take > tbw ? min(take - tbw, tw) : 0u;
+        const double kw = s_wmass[lane] + (double)mw * pstar;
+        const double kbw = cbefore + excl_d(kw);
+        const unsigned cw = __ballot_sync(kFull, kw > 0.0 && kbw <= threshold);
+        if (cw) {
+          walk = 31 - __clz(cw);
+          walk_before = __shfl_sync(kFull, kbw, walk);
+          walk_rank = __shfl_sync(kFull, tbw, walk);
         }
+      }
+      if (lane == 0) {
+        s_walk_warp = walk;
+        s_walk_before = walk_before;
+        s_walk_rank = walk_rank;
       }
     }
     __syncthreads();
@@ -713,10 +773,9 @@ __global__ void __launch_bounds__(kCsThreads, 1)
             uint32_t above_bits = 0u, tie_bits = 0u;
 #pragma unroll
             for (int t = 0; t < 8; ++t) {
-              if (!((m >> t) & 1u) || v[t] == -INFINITY) continue;
-              const uint32_t o = ord32(v[t]);
-              if (o > vstar) above_bits |= 1u << t;
-              if (o == vstar && !keep_all) tie_bits |= 1u << t;
+              if (!((m >> t) & 1u)) continue;
+              if (v[t] > vstar_f) above_bits |= 1u << t;
+              if (v[t] == vstar_f) tie_bits |= 1u << t;
             }
             // ranks of this lane's ties among the row's ties, in id order
             const uint32_t c = __popc(tie_bits);

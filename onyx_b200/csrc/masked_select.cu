@@ -1569,7 +1569,7 @@ static int launch_cluster_sample(int dtype, const SampleParams& sp, int dev, cud
   struct DevInfo {
     bool ready = false;
     int sms = 0, max_dyn = 0;
-    int fits[3][kCsMaxCluster + 1];  // per dtype and k: -1 unknown, 0 no, 1 yes (occupancy)
+    int fits[3][kCsMaxCluster + 1];  // per dtype and k: resident clusters, -1 not yet asked
   };
   static std::mutex mu;
   static DevInfo info[64];
@@ -1611,13 +1611,12 @@ static int launch_cluster_sample(int dtype, const SampleParams& sp, int dev, cud
   int64_t k_par = d.sms / std::max<int64_t>(1, sp.rows);
   k_par = std::min<int64_t>(k_par, (sp.vocab + 4095) / 4096);
   if (forced_k) k_par = forced_k;
-  int k = (int)std::max<int64_t>(k_fit, std::min<int64_t>(k_par, kCsMaxCluster));
-  if ((int64_t)k * sp.rows > 0x7FFFFFFFll) return kNoClusterPlan;
-  for (;; --k) {
-    if (k < k_fit) return kNoClusterPlan;
-    const ClusterSamplePlan pl = cs_layout(k, sp.vocab, elem, masked);
-    int& fits = d.fits[di][k];
-    if (fits < 0) {
+  const int k0 = (int)std::max<int64_t>(k_fit, std::min<int64_t>(k_par, kCsMaxCluster));
+  if ((int64_t)k0 * sp.rows > 0x7FFFFFFFll) return kNoClusterPlan;
+  // clusters that can be resident at once for k CTAs per row (cached per dtype and k)
+  auto active = [&](int k) {
+    int& n = d.fits[di][k];
+    if (n < 0) {
       cudaLaunchConfig_t q = {};
       cudaLaunchAttribute qa[1];
       qa[0].id = cudaLaunchAttributeClusterDimension;
@@ -1632,9 +1631,25 @@ static int launch_cluster_sample(int dtype, const SampleParams& sp, int dev, cud
       int clusters = 0;
       const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, fn, &q);
       if (e != cudaSuccess) (void)cudaGetLastError();
-      fits = (e == cudaSuccess && clusters > 0) ? 1 : 0;
+      n = e == cudaSuccess ? clusters : 0;
     }
-    if (!fits) continue;
+    return n;
+  };
+  // candidates: k0, then the powers of two below it (down to k_fit); the first that holds
+  // every row's cluster at once, else the smallest that runs at all
+  int cand[8], nc = 0;
+  cand[nc++] = k0;
+  if (!forced_k)
+    for (int kk = 8; kk >= 1; kk >>= 1)
+      if (kk < k0 && kk >= k_fit) cand[nc++] = kk;
+  int k = 0;
+  for (int i = 0; i < nc && !k; ++i)
+    if (active(cand[i]) >= sp.rows) k = cand[i];
+  for (int i = nc - 1; i >= 0 && !k; --i)
+    if (active(cand[i]) >= 1) k = cand[i];
+  if (!k) return kNoClusterPlan;
+  {
+    const ClusterSamplePlan pl = cs_layout(k, sp.vocab, elem, masked);
     ClusterSampleParams cp = {};
     cp.logits = sp.logits;
     cp.row_stride = sp.row_stride;
