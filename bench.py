@@ -8,7 +8,7 @@ replayed from CUDA graphs.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload batched|spec_verify|table_gather|scaling|vocab_parallel|
-                                dfa_masks|sample]
+                                dfa_masks|sample|grammar_row]
 
 One process per GPU (torchrun for N > 1). Batches shard over ranks with no communication
 ("weak" scaling) except ``vocab_parallel``, which splits the vocabulary and all-gathers
@@ -59,6 +59,10 @@ WORKLOADS = {
                     desc="batch-sharded masked argmax bf16 [128/GPU,256000] at 5% density"),
     "vocab_parallel": dict(rows=1024, vocab=256000,
                            desc="vocabulary-sharded masked argmax bf16 [1024,256000/N] + NCCL all-gather"),
+    "grammar_row": dict(rows=1, vocab=32000,
+                        desc="one fp32 row [1,32000] under the grammar [0-9]{1,8} at its initial "
+                             "state: the valid-token mask built on the GPU from the DFA state, "
+                             "then the masked argmax"),
     "sample": dict(rows=64, vocab=128256, temperature=0.8, top_p=0.9,
                    desc="masked temperature / top-p sampling bf16 [64,128256], mask u32 [64,4008], "
                         "T=0.8, top_p=0.9"),
@@ -79,6 +83,8 @@ def bytes_per_row(name: str, world: int = 1) -> float:
         return words * 4 + 4 + v * 2 + 8
     if name == "vocab_parallel":
         return (v * 2 + words * 4) / world + 8 + 8
+    if name == "grammar_row":  # one f32 row, its mask words, the output
+        return v * 4 + words * 4 + 4
     if name == "dfa_masks":  # per state row: its mask words written, plus its share of the
         # vocabulary read once per step (offsets 8 B/token, about 5 token bytes/token)
         return words * 4 + 4 + (v * 8 + v * 5) / w["rows"]
@@ -213,6 +219,25 @@ def cpu_measure(name: str, budget_s: float, steps: int | None = None, warmup: in
 
         rows_per_call = w["logits_bf16"].shape[0]
         what = "spec verify of 32 entries x 5 rows x 151936 bf16"
+    elif name == "grammar_row":
+        from types import SimpleNamespace
+
+        from onyx_b200 import workloads
+
+        w = workloads.single_row()
+        d = workloads.digits_dfa(8)
+        dfa = SimpleNamespace(trans=d["trans"], dead=d["dead"])
+        threads = 1  # one row: the scan and the selection run on one thread
+
+        packed = oracle.pack_vocabulary(w["vocabulary"])  # once, as the reference holds its vocabulary
+
+        def run_once():
+            words = oracle.dfa_scan_bitmask(dfa, d["start"], w["vocabulary"], packed=packed)
+            oracle.masked_argmax(w["logits"], words[None], dtype="f32", threads=1)
+
+        rows_per_call = 1
+        what = ("valid-token scan of 32000 tokens + masked argmax of one f32 row "
+                "(the C oracle, one thread)")
     elif name == "sample":
         from oracle import sampling as osamp
         from onyx_b200 import workloads
@@ -290,7 +315,7 @@ def run_reference(args) -> None:
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "u32" if args.workload == "dfa_masks" else "bf16",
+        "dtype": {"dfa_masks": "u32", "grammar_row": "f32"}.get(args.workload, "bf16"),
         "data": "synthetic (seeded, shapes and distributions of the workload)",
         "config": {"workload": args.workload, "desc": WORKLOADS[args.workload]["desc"]},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
@@ -702,6 +727,144 @@ def run_dfa_masks(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_grammar_row(args) -> None:
+    """One-row grammar leg: each step builds the row's valid-token mask on the GPU from the
+    DFA state (the reference's per-step scan) and selects the masked argmax of one fp32 row:
+    two launches. Logits rows rotate through more than twice the L2; the vocabulary and the
+    DFA table stay resident by design. One GPU; N > 1 replicas (weak)."""
+    import torch
+    import torch.distributed as dist
+
+    from onyx_b200 import dfa_masks
+    from onyx_b200 import masked_selection as ms
+    from onyx_b200 import workloads
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    spec = WORKLOADS["grammar_row"]
+    w = workloads.single_row()
+    d = workloads.digits_dfa(8)
+    builder = dfa_masks.DfaMaskBuilder(d["trans"], d["dead"], w["vocabulary"], device=dev)
+    V = spec["vocab"]
+    props = torch.cuda.get_device_properties(dev)
+    l2 = int(getattr(props, "L2_cache_size", 126 * 2**20))
+    R = math.ceil(2 * l2 / (V * 4)) + 1
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(workloads.SEEDS[1] + 17 * rank)
+    X = torch.randn((R, V), generator=gen, device=dev, dtype=torch.float32) * 3.0
+    X[0].copy_(torch.from_numpy(w["logits"][0]).to(dev))
+    states = torch.full((1,), d["start"], dtype=torch.int32, device=dev)
+
+    def step(k: int):
+        m = builder.masks(states)
+        return ms.masked_argmax(X[k % R : k % R + 1], m)
+
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for k in range(max(3, args.warmup)):
+            step(k)
+    stream.synchronize()
+    chunk = min(args.steps, 1024)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for k in range(chunk):
+            step(k)
+    with torch.cuda.stream(stream):
+        graph.replay()
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        done = 0
+        with torch.cuda.stream(stream):
+            while done < args.steps:
+                graph.replay()
+                done += chunk
+        end.record(stream)
+        end.synchronize()
+    t = torch.tensor([start.elapsed_time(end) / done], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_step = float(t.item())
+    value = world / (ms_per_step / 1e3)
+    peak, peak_kind = _peaks()
+    per_launch = bytes_per_row("grammar_row")
+    achieved = per_launch / (ms_per_step / 1e3) / 1e9
+
+    # end to end: the row and the state id up, the token id and status down, every step
+    pinned_x = torch.from_numpy(w["logits"]).pin_memory()
+    pinned_s = torch.full((1,), d["start"], dtype=torch.int32).pin_memory()
+    host_out = torch.empty((2, 1), dtype=torch.int32).pin_memory()
+    dev_x = torch.empty((1, V), dtype=torch.float32, device=dev)
+    dev_s = torch.empty(1, dtype=torch.int32, device=dev)
+
+    def e2e_step():
+        dev_x.copy_(pinned_x, non_blocking=True)
+        dev_s.copy_(pinned_s, non_blocking=True)
+        r = ms.masked_argmax(dev_x, builder.masks(dev_s))
+        host_out[0].copy_(r.token_ids, non_blocking=True)
+        host_out[1].copy_(r.status, non_blocking=True)
+
+    e2e_steps = min(args.steps, 2000)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            e2e_step()
+    stream.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        b.record(stream)
+    b.synchronize()
+    e2e_value = e2e_steps * world / (a.elapsed_time(b) / 1e3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, threads, sample, _, _ = cpu_measure("grammar_row", budget_s=args.cpu_seconds)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": "grammar_row rows/s", "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": done, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "us_per_row": ms_per_step * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,3) f32 logits; synthetic 32,000-token vocabulary; "
+                "the grammar [0-9]{1,8})",
+        "config": {"workload": "grammar_row", "desc": spec["desc"], "rows_per_step_per_gpu": 1,
+                   "parallelism": f"replicas x{world}",
+                   "l2_policy": f"{R} rotating logits rows ({R * V * 4 / 1e6:.0f} MB > 2 x L2); "
+                                "vocabulary and DFA table resident by design",
+                   "timing": "CUDA events on the launching stream, CUDA-graph replay, "
+                             "2 launches per step (mask producer, masked argmax)"},
+        "gbs": achieved,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "peak_source": f"MEASURED_PEAKS.json hbm_gbs (of {peak_kind})",
+                     "algorithmic_bytes_per_launch": per_launch},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": V * 4 + 4,
+                "d2h_bytes_per_step": 8, "steps": e2e_steps},
+        "cpu_baseline": cpu,
+        "gpu_launches": done * 2,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -722,6 +885,8 @@ def main() -> None:
         run_reference(args)
     elif args.workload == "dfa_masks":
         run_dfa_masks(args)
+    elif args.workload == "grammar_row":
+        run_grammar_row(args)
     else:
         run_ours(args)
 

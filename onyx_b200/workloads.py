@@ -112,6 +112,32 @@ def synthetic_dfa(rng: np.random.Generator, states: int = 64, live: float = 0.2)
     return {"trans": trans, "dead": 0, "start": 1}
 
 
+def digits_dfa(max_len: int = 8) -> dict:
+    """Dense byte DFA of the anchored pattern ``[0-9]{1,max_len}`` as the reference's
+    leftmost-first dense DFA behaves (matches reported one byte late), built directly:
+
+    * 0 dead; 1 start; 1 + j after j digits (j = 1..max_len); ``m`` = max_len + 2, the
+      delayed-match state a match that has ended moves to on any byte;
+    * start: digit -> 2, anything else -> dead;
+    * after j < max_len digits: digit -> j + 1 digits, anything else -> m;
+    * after max_len digits: any byte -> m;  m: any byte -> dead.
+
+    So a token is valid from the start state iff it is d^j (1 <= j <= max_len) or d^j followed
+    by one more byte of any kind."""
+    n = max_len + 3
+    m = max_len + 2
+    trans = np.zeros((n, 256), np.int32)
+    digits = np.arange(ord("0"), ord("9") + 1)
+    trans[1, digits] = 2
+    for j in range(1, max_len + 1):
+        s = 1 + j
+        trans[s, :] = m
+        if j < max_len:
+            trans[s, digits] = s + 1
+    trans[m, :] = 0
+    return {"trans": trans, "dead": 0, "start": 1}
+
+
 def single_row(seed: int = SEEDS[1]) -> dict:
     rng = np.random.default_rng(seed)
     vocabulary = synthetic_vocabulary(rng, 32000)

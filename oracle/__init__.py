@@ -214,10 +214,11 @@ def pack_vocabulary(vocabulary) -> tuple[np.ndarray, np.ndarray]:
     return data, offsets
 
 
-def dfa_scan_bitmask(dfa, state: int, vocabulary) -> np.ndarray:
-    """Packed valid-token bitmask of ``state`` (restating get_valid_token_ids)."""
+def dfa_scan_bitmask(dfa, state: int, vocabulary, *, packed=None) -> np.ndarray:
+    """Packed valid-token bitmask of ``state`` (restating get_valid_token_ids). ``packed``:
+    ``pack_vocabulary(vocabulary)`` done once by the caller, for repeated scans."""
     lib = load()
-    data, offsets = pack_vocabulary(vocabulary)
+    data, offsets = packed if packed is not None else pack_vocabulary(vocabulary)
     trans = np.ascontiguousarray(dfa.trans, dtype=np.int32)
     V = len(vocabulary)
     out = np.zeros((V + 31) // 32, np.uint32)

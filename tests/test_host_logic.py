@@ -200,3 +200,29 @@ def test_dfa_mask_host_helpers():
         dfa_masks.DfaMaskBuilder(trans, 0, [])
     with pytest.raises(ValueError):
         dfa_masks.DfaMaskBuilder(trans, 0, [b"a"], device="cpu")
+
+
+def test_digits_dfa_matches_the_restated_regex_compiler():
+    """The config-1 grammar's table, built directly in workloads, gives the same valid-token
+    sets as the oracle's compile of [0-9]{1,8} (state numbering aside): from the start
+    state over the synthetic 32,000-token vocabulary and over hand-picked tokens, and after
+    every prefix of digits."""
+    from types import SimpleNamespace
+
+    from oracle.regex_dfa import compile_regex_dfa
+
+    ref = compile_regex_dfa("[0-9]{1,8}")
+    d = workloads.digits_dfa(8)
+    mine = SimpleNamespace(trans=d["trans"], dead=d["dead"])
+    vocab = workloads.single_row()["vocabulary"] + [
+        b"5", b"5a", b"5ab", b"12345678", b"123456789", b"1234567890", b"a", b"0x", b"00", b"9 ",
+    ]
+    assert np.array_equal(oracle.dfa_scan_bitmask(mine, d["start"], vocab),
+                          oracle.dfa_scan_bitmask(ref, ref.start, vocab))
+    for k in range(1, 9):
+        s_ref = ref.walk(ref.start, b"7" * k)
+        s_mine = d["start"]
+        for b in b"7" * k:
+            s_mine = int(d["trans"][s_mine, b])
+        assert np.array_equal(oracle.dfa_scan_bitmask(mine, s_mine, vocab),
+                              oracle.dfa_scan_bitmask(ref, s_ref, vocab))
