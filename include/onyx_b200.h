@@ -181,7 +181,8 @@ ONYX_API int onyx_masked_sample(const void* logits, int dtype, int64_t rows, int
  * `dead_absorbing` nonzero promises every transition from `dead` returns to it (true of
  * regex-automata's dense DFAs) and lets walks stop there. Out-of-range transitions count as
  * dead, out-of-range state ids give empty rows, and offsets outside the byte array give empty
- * tokens, so malformed input is never read out of bounds.
+ * tokens, so malformed input is never read out of bounds. n_states is at most 2^23 (8 GB
+ * of table); beyond it the call returns ONYX_ERR_INVALID_ARGUMENT.
  */
 ONYX_API int onyx_dfa_state_masks(const int32_t* trans, int32_t n_states, int32_t dead,
                                   int dead_absorbing, const int32_t* states, int64_t rows,

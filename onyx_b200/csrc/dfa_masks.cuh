@@ -71,30 +71,35 @@ __global__ void __launch_bounds__(kDfaWarpsPerBlock * 32) dfa_mask_kernel(const 
       s[j] = ok ? st : d.dead;
       live[j] = ok && len > 0 && !(d.dead_absorbing && st == d.dead);
     }
-    for (int64_t i = 0; i < len; ++i) {
-      bool any = false;
-#pragma unroll
-      for (int j = 0; j < kDfaLockstep; ++j) any |= live[j];
-      if (!any) break;
-      uint32_t b;
-      if (i < kDfaCachedBytes) {
-        uint32_t w = cached[0];
-#pragma unroll
-        for (int q = 1; q < kDfaCachedBytes / 4; ++q)
-          if ((i >> 2) == q) w = cached[q];
-        b = (w >> (8 * (i & 3))) & 0xFFu;
-      } else {
-        b = __ldg(d.tok_bytes + a + i);
-      }
+    // one byte of every live walk: 32-bit table offsets (the host bounds n_states * 256
+    // below 2^31); an entry outside the table is the dead state
+    auto step = [&](uint32_t b) {
 #pragma unroll
       for (int j = 0; j < kDfaLockstep; ++j) {
         if (!live[j]) continue;
-        int32_t nx = __ldg(d.trans + (int64_t)s[j] * 256 + b);
-        if (nx < 0 || nx >= d.n_states) nx = d.dead;  // malformed table: dead, never out of bounds
+        int32_t nx = __ldg(d.trans + (((uint32_t)s[j] << 8) | b));
+        if ((uint32_t)nx >= (uint32_t)d.n_states) nx = d.dead;
         s[j] = nx;
         if (d.dead_absorbing && nx == d.dead) live[j] = false;
       }
+    };
+    auto any_live = [&]() {
+      bool any = false;
+#pragma unroll
+      for (int j = 0; j < kDfaLockstep; ++j) any |= live[j];
+      return any;
+    };
+    // the cached bytes four at a time (fixed shifts), then any longer tail from memory
+    const int lc = (int)min(len, (int64_t)kDfaCachedBytes);
+#pragma unroll
+    for (int q = 0; q < kDfaCachedBytes / 4; ++q) {
+      if (q * 4 >= lc || !any_live()) break;
+      const uint32_t w = cached[q];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (q * 4 + k < lc) step((w >> (8 * k)) & 0xFFu);
     }
+    for (int64_t i = kDfaCachedBytes; i < len && any_live(); ++i) step(__ldg(d.tok_bytes + a + i));
 #pragma unroll
     for (int j = 0; j < kDfaLockstep; ++j) {
       const int64_t r = rg + j;

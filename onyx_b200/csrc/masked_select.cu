@@ -1764,9 +1764,10 @@ int onyx_dfa_state_masks(const int32_t* trans, int32_t n_states, int32_t dead,
                          int dead_absorbing, const int32_t* states, int64_t rows,
                          const uint8_t* tok_bytes, int64_t n_bytes, const int64_t* tok_offsets,
                          int64_t vocab, uint32_t* out, int64_t out_stride, void* stream) {
-  if (!trans || n_states < 1 || dead < 0 || dead >= n_states || rows < 0 || vocab < 1 ||
-      vocab > 0x7FFFFFFFll - 1 || !tok_offsets || n_bytes < 0 || (n_bytes > 0 && !tok_bytes) ||
-      out_stride < (vocab + 31) / 32)
+  // n_states * 256 table entries are addressed with 32-bit offsets
+  if (!trans || n_states < 1 || n_states > (1 << 23) || dead < 0 || dead >= n_states ||
+      rows < 0 || vocab < 1 || vocab > 0x7FFFFFFFll - 1 || !tok_offsets || n_bytes < 0 ||
+      (n_bytes > 0 && !tok_bytes) || out_stride < (vocab + 31) / 32)
     return ONYX_ERR_INVALID_ARGUMENT;
   if (rows == 0) return ONYX_OK;
   if (!states || !out) return ONYX_ERR_INVALID_ARGUMENT;
