@@ -801,6 +801,31 @@ def run_grammar_row(args) -> None:
     per_launch = bytes_per_row("grammar_row")
     achieved = per_launch / (ms_per_step / 1e3) / 1e9
 
+    # the table path, for context: every state's mask built once, then one gather launch per
+    # step (the state id selects the row's mask from the table)
+    table = builder.table()
+    g_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        for k in range(3):
+            ms.gather_masked_argmax(X[k % R : k % R + 1], table, states)
+    stream.synchronize()
+    with torch.cuda.graph(g_graph, stream=stream):
+        for k in range(chunk):
+            ms.gather_masked_argmax(X[k % R : k % R + 1], table, states)
+    with torch.cuda.stream(stream):
+        g_graph.replay()
+    stream.synchronize()
+    ta, tb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ta.record(stream)
+    g_done = 0
+    with torch.cuda.stream(stream):
+        while g_done < args.steps:
+            g_graph.replay()
+            g_done += chunk
+    tb.record(stream)
+    tb.synchronize()
+    table_us = ta.elapsed_time(tb) / g_done * 1e3
+
     # end to end: the row and the state id up, the token id and status down, every step
     pinned_x = torch.from_numpy(w["logits"]).pin_memory()
     pinned_s = torch.full((1,), d["start"], dtype=torch.int32).pin_memory()
@@ -842,6 +867,7 @@ def run_grammar_row(args) -> None:
         "metric": "grammar_row rows/s", "value": value, "unit": UNIT, "n_gpus": world,
         "steps": done, "warmup": args.warmup, "ms_per_step": ms_per_step,
         "us_per_row": ms_per_step * 1e3,
+        "table_path_us_per_row": table_us,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,3) f32 logits; synthetic 32,000-token vocabulary; "
                 "the grammar [0-9]{1,8})",
