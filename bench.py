@@ -38,11 +38,16 @@ sys.path.insert(0, str(ROOT))
 METRIC = "masked-argmax rows/s and HBM GB/s (vs ~8 TB/s), B=64 V=128256 bf16"
 UNIT = "rows/s"
 
-# dram__bytes_read.sum + dram__bytes_write.sum per launch from an ncu capture of the
-# dominant kernel (profiles/masked_select_batched_bf16.md).
-NCU_TRAFFIC_PER_LAUNCH: dict[str, float | None] = {"batched": 17458688.0}
-
 FALLBACK_HBM_GBS = 6650.0
+
+# GPU-side delay (SM clock cycles, about 5 ms) enqueued just before the start event of a
+# timed region: the host enqueues the timed graph replays while the GPU spins, so the
+# region holds the steps back to back and none of the host's launch latency.
+DELAY_CYCLES = 10_000_000
+
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of each workload's dominant
+# kernel, from a single-launch ncu capture of the current kernels (absent: not captured)
+NCU_TRAFFIC_PER_LAUNCH: dict[str, float] = {}
 
 
 # ---------------------------------------------------------------------------------------
@@ -91,6 +96,34 @@ def bytes_per_row(name: str, world: int = 1) -> float:
     return v * 2 + words * 4 + 8
 
 
+L2_POLICY = {
+    "dfa_masks": "inputs (the vocabulary and the DFA table) stay in L2 by design: the walk is "
+                 "latency-bound and the masks are written once per step",
+    "grammar_row": "logits rows rotate through distinct buffers totalling more than 2 x L2; "
+                   "the vocabulary and the DFA table stay resident by design",
+}
+
+
+def workload_config(name: str, world: int, exchange: str) -> dict:
+    """The ``config`` object of a JSON line; both arms print the same one."""
+    spec = WORKLOADS[name]
+    if name == "vocab_parallel":
+        par = f"vocab-sharded x{world}, keys exchanged by " + (
+            "NVLink peer stores" if exchange == "peer" else "NCCL all-gather")
+    elif name in ("dfa_masks", "grammar_row"):
+        par = f"replicas x{world}"
+    else:
+        par = f"batch-sharded x{world}"
+    return {
+        "workload": name,
+        "desc": spec["desc"],
+        "rows_per_step_per_gpu": spec["rows"],
+        "parallelism": par,
+        "l2_policy": L2_POLICY.get(
+            name, "input sets rotate through distinct device buffers totalling more than 2 x L2"),
+    }
+
+
 # ---------------------------------------------------------------------------------------
 def _peaks() -> tuple[float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
@@ -101,10 +134,20 @@ def _peaks() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback"
 
 
-class ClockSampler:
-    """Samples SM clock and throttle reasons through NVML while the timed region runs."""
+def gpu_delay(stream) -> None:
+    """Keep the GPU busy on ``stream`` for about DELAY_CYCLES SM cycles (a spin kernel), so
+    that work the host enqueues next starts back to back once the delay ends."""
+    import torch
 
-    def __init__(self, device_index: int, period_s: float = 0.0005) -> None:
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(DELAY_CYCLES)
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while the timed region runs (from
+    the GPU-side delay before its start event to its end)."""
+
+    def __init__(self, device_index: int, period_s: float = 0.001) -> None:
         self.samples: list[tuple[int, int]] = []
         self.period = period_s
         self._stop = threading.Event()
@@ -201,9 +244,12 @@ def _cpu_inputs(name: str):
     raise ValueError(name)
 
 
-def cpu_measure(name: str, budget_s: float, steps: int | None = None, warmup: int = 0):
+def cpu_measure(name: str, budget_s: float, steps: int | None = None, warmup: int = 0,
+                min_seconds: float = 1.0):
     """Time the oracle (C, OpenMP over rows, all usable cores) on this workload.
 
+    With ``steps``: whole blocks of ``steps`` calls until at least ``min_seconds`` have
+    passed (or ``budget_s``). Without: calls until ``budget_s``.
     Returns (rows/s, threads, sample description, seconds, rows processed)."""
     import oracle
 
@@ -287,7 +333,8 @@ def cpu_measure(name: str, budget_s: float, steps: int | None = None, warmup: in
         n += 1
         el = time.perf_counter() - t0
         if steps is not None:
-            if n >= steps or el > budget_s:
+            # whole blocks of `steps` calls, until at least min_seconds of work (or the budget)
+            if (n % steps == 0 and el >= min_seconds) or el > budget_s:
                 break
         elif el > budget_s and n >= 2:
             break
@@ -300,10 +347,12 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    # bounded: each step is one call over the workload's batch; the run stops early once
-    # about 60 s of CPU work is done, so any --steps finishes within minutes
+    # bounded: each step is one call over the workload's batch; whole blocks of --steps
+    # calls run until at least 1 s of CPU work is timed, and the run stops early once about
+    # 60 s of CPU work is done, so any --steps finishes within minutes
     value, threads, sample, el, rows = cpu_measure(args.workload, budget_s=60.0,
-                                                   steps=args.steps, warmup=min(args.warmup, 3))
+                                                   steps=args.steps, warmup=min(args.warmup, 3),
+                                                   min_seconds=1.0)
     line = {
         "impl": "reference",
         "metric": METRIC if args.workload == "batched" else f"{args.workload} rows/s",
@@ -317,7 +366,9 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": {"dfa_masks": "u32", "grammar_row": "f32"}.get(args.workload, "bf16"),
         "data": "synthetic (seeded, shapes and distributions of the workload)",
-        "config": {"workload": args.workload, "desc": WORKLOADS[args.workload]["desc"]},
+        "config": workload_config(args.workload, args.gpus, args.exchange),
+        "timing": "wall clock (perf_counter) around whole blocks of --steps calls on the host "
+                  "cores, at least 1 s",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -474,6 +525,7 @@ def run_ours(args) -> None:
         dist.barrier()
     torch.cuda.synchronize(dev)
     with ClockSampler(local) as clocks:
+        gpu_delay(stream)
         start.record(stream)
         if use_graphs:
             with torch.cuda.stream(stream):
@@ -522,47 +574,61 @@ def run_ours(args) -> None:
         return v.view(np.int32) if v.dtype == np.uint32 else v
 
     pinned = {k: torch.from_numpy(_host_view(k, v)).pin_memory() for k, v in host_in.items()}
-    out_host = torch.empty((2, rows_per_step), dtype=torch.int32).pin_memory()
-    dev_in = {k: torch.empty(v.shape, dtype=v.dtype, device=dev) for k, v in pinned.items()}
+    # two device input sets and two pinned result buffers: step k+1's inputs are copied on
+    # their own stream while step k's kernel and read-back run
+    out_host = [torch.empty((2, rows_per_step), dtype=torch.int32).pin_memory() for _ in range(2)]
+    dev_in = [{k: torch.empty(v.shape, dtype=v.dtype, device=dev) for k, v in pinned.items()}
+              for _ in range(2)]
     h2d = sum(v.numel() * v.element_size() for v in pinned.values())
-    d2h = out_host.numel() * 4
+    d2h = out_host[0].numel() * 4
+    copy_stream = torch.cuda.Stream(dev)
+    copied = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        for k, v in pinned.items():
-            dev_in[k].copy_(v, non_blocking=True)
-        xin = dev_in["x"].view(torch.bfloat16)
-        if name in ("batched", "scaling"):
-            r = ms.masked_argmax(xin, dev_in["m"])
-            out = (r.token_ids, r.status)
-        elif name == "table_gather":
-            r = ms.gather_masked_argmax(xin, table, dev_in["ids"])
-            out = (r.token_ids, r.status)
-        elif name == "sample":
-            r = sampling.masked_sample(xin, dev_in["m"], temperature=spec["temperature"],
-                                       top_p=spec["top_p"], seed=1234 + rank, call=0)
-            out = (r.token_ids, r.status)
-        elif name == "spec_verify":
-            r = ms.spec_verify(xin, dev_in["m"], dev_in["d"])
-            out = (r.accept_len, r.correction)
-        else:
-            r = vocab_parallel.vocab_parallel_masked_argmax(xin, dev_in["m"], col_offset,
-                                                            exchange=exchange)
-            out = (r.token_ids, r.status)
-        out_host[0].copy_(out[0], non_blocking=True)
-        out_host[1].copy_(out[1], non_blocking=True)
+    def e2e_step(k: int):
+        j = k & 1
+        with torch.cuda.stream(copy_stream):
+            if k >= 2:  # the kernel of step k-2 has finished reading this input set
+                copy_stream.wait_event(consumed[j])
+            for key, v in pinned.items():
+                dev_in[j][key].copy_(v, non_blocking=True)
+            copied[j].record(copy_stream)
+        stream.wait_event(copied[j])
+        with torch.cuda.stream(stream):
+            d = dev_in[j]
+            xin = d["x"].view(torch.bfloat16)
+            if name in ("batched", "scaling"):
+                r = ms.masked_argmax(xin, d["m"])
+                out = (r.token_ids, r.status)
+            elif name == "table_gather":
+                r = ms.gather_masked_argmax(xin, table, d["ids"])
+                out = (r.token_ids, r.status)
+            elif name == "sample":
+                r = sampling.masked_sample(xin, d["m"], temperature=spec["temperature"],
+                                           top_p=spec["top_p"], seed=1234 + rank, call=0)
+                out = (r.token_ids, r.status)
+            elif name == "spec_verify":
+                r = ms.spec_verify(xin, d["m"], d["d"])
+                out = (r.accept_len, r.correction)
+            else:
+                r = vocab_parallel.vocab_parallel_masked_argmax(xin, d["m"], col_offset,
+                                                                exchange=exchange)
+                out = (r.token_ids, r.status)
+            consumed[j].record(stream)
+            out_host[j][0].copy_(out[0], non_blocking=True)
+            out_host[j][1].copy_(out[1], non_blocking=True)
 
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            e2e_step()
-    stream.synchronize()
+    for k in range(3):
+        e2e_step(k)
+    torch.cuda.synchronize(dev)
     if distributed:
         dist.barrier()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e_start.record(stream)
-        for _ in range(e2e_steps):
-            e2e_step()
-        e_end.record(stream)
+    e_start.record(copy_stream)
+    stream.wait_stream(copy_stream)
+    for k in range(e2e_steps):
+        e2e_step(k)
+    e_end.record(stream)
     e_end.synchronize()
     et = torch.tensor([e_start.elapsed_time(e_end)], dtype=torch.float64, device=dev)
     if distributed:
@@ -597,18 +663,10 @@ def run_ours(args) -> None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,3) bf16 logits, Bernoulli token bitmasks)",
-        "config": {
-            "workload": name,
-            "desc": spec["desc"],
-            "rows_per_step_per_gpu": rows_per_step,
-            "parallelism": (f"batch-sharded x{world}" if name != "vocab_parallel"
-                            else f"vocab-sharded x{world}, keys exchanged by "
-                                 + ("NVLink peer stores" if exchange is not None
-                                    else "NCCL all-gather")),
-            "l2_policy": f"{R} rotating input sets ({R * set_bytes / 1e6:.0f} MB > 2 x L2 "
-                         f"{l2 / 1e6:.0f} MB)",
-            "timing": "CUDA events on the launching stream, CUDA-graph replay of the steps, max over ranks",
-        },
+        "config": workload_config(name, world, args.exchange),
+        "l2_rotation": f"{R} input sets ({R * set_bytes / 1e6:.0f} MB > 2 x L2 {l2 / 1e6:.0f} MB)",
+        "timing": "CUDA events on the launching stream around K graph-replayed steps enqueued "
+                  "behind a GPU-side delay, max over ranks",
         "gbs": achieved,
         "roofline": roofline,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
@@ -661,6 +719,7 @@ def run_dfa_masks(args) -> None:
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        gpu_delay(stream)
         start.record(stream)
         done = 0
         with torch.cuda.stream(stream):
@@ -708,11 +767,9 @@ def run_dfa_masks(args) -> None:
         "steps": done, "warmup": args.warmup, "ms_per_step": ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u32",
         "data": "synthetic (seeded 64-state DFA, 20% live transitions; synthetic vocabulary)",
-        "config": {"workload": "dfa_masks", "desc": spec["desc"], "rows_per_step_per_gpu": R,
-                   "parallelism": f"replicas x{world}",
-                   "l2_policy": "inputs (1.7 MB vocabulary) stay in L2 by design: the walk is "
-                                "latency-bound, the output is written once per step",
-                   "timing": "CUDA events on the launching stream, CUDA-graph replay"},
+        "config": workload_config("dfa_masks", world, args.exchange),
+        "timing": "CUDA events on the launching stream around graph-replayed steps enqueued "
+                  "behind a GPU-side delay",
         "gbs": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": None,
@@ -784,6 +841,7 @@ def run_grammar_row(args) -> None:
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        gpu_delay(stream)
         start.record(stream)
         done = 0
         with torch.cuda.stream(stream):
@@ -816,6 +874,7 @@ def run_grammar_row(args) -> None:
         g_graph.replay()
     stream.synchronize()
     ta, tb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gpu_delay(stream)
     ta.record(stream)
     g_done = 0
     with torch.cuda.stream(stream):
@@ -871,12 +930,10 @@ def run_grammar_row(args) -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,3) f32 logits; synthetic 32,000-token vocabulary; "
                 "the grammar [0-9]{1,8})",
-        "config": {"workload": "grammar_row", "desc": spec["desc"], "rows_per_step_per_gpu": 1,
-                   "parallelism": f"replicas x{world}",
-                   "l2_policy": f"{R} rotating logits rows ({R * V * 4 / 1e6:.0f} MB > 2 x L2); "
-                                "vocabulary and DFA table resident by design",
-                   "timing": "CUDA events on the launching stream, CUDA-graph replay, "
-                             "2 launches per step (mask producer, masked argmax)"},
+        "config": workload_config("grammar_row", world, args.exchange),
+        "l2_rotation": f"{R} logits rows ({R * V * 4 / 1e6:.0f} MB > 2 x L2)",
+        "timing": "CUDA events on the launching stream around graph-replayed steps enqueued "
+                  "behind a GPU-side delay; 2 launches per step (mask producer, masked argmax)",
         "gbs": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": None,

@@ -75,6 +75,38 @@ ONYX_API const char* onyx_error_string(int code);
 ONYX_API int onyx_last_cuda_error(void);
 
 /*
+ * Process-wide diagnostic and test options. None is needed in normal use; each starts from
+ * an environment variable read once, at the first call that uses any option, and changes
+ * only through onyx_set_option (which returns ONYX_ERR_INVALID_ARGUMENT for an unknown id
+ * or value). Options apply to launches made after the change. No counterpart in the
+ * reference (its selection is plain PyTorch).
+ *   CLUSTER      1: rows that fit one thread-block cluster use the cluster kernel;
+ *                0: the global-ticket merge instead (ONYX_B200_CLUSTER, default 1).
+ *   PDL          1: launches allow programmatic dependent launch (ONYX_B200_PDL, default 1).
+ *   STREAM       when the streaming form (one CTA per SM, shared-memory ring fed by bulk
+ *                copies) selects: ONYX_STREAM_NEVER, ONYX_STREAM_ALWAYS (every shape it can
+ *                serve), ONYX_STREAM_AUTO (batches of several waves; ONYX_B200_STREAM,
+ *                default AUTO).
+ *   SAMPLE_FORM  masked sampling: 0 the cluster form with the cluster size chosen from the
+ *                batch, -1 the one-CTA form, k in [1, 16] clusters of k CTAs
+ *                (ONYX_B200_SAMPLE_FORM: "single" or "cluster:<k>", default 0).
+ *   TEST_WITHHELD_KEY_BYTES  test hook, 0 in normal use: rank 0 of a cluster expects this
+ *                many key bytes beyond those its CTAs send, so its bounded wait runs out
+ *                and the rows report ONYX_STATUS_WAIT_TIMEOUT. Set only by tests.
+ */
+#define ONYX_OPTION_CLUSTER 0
+#define ONYX_OPTION_PDL 1
+#define ONYX_OPTION_STREAM 2
+#define ONYX_OPTION_SAMPLE_FORM 3
+#define ONYX_OPTION_TEST_WITHHELD_KEY_BYTES 4
+#define ONYX_OPTION_COUNT 5
+#define ONYX_STREAM_NEVER 0
+#define ONYX_STREAM_ALWAYS 1
+#define ONYX_STREAM_AUTO 2
+ONYX_API int onyx_set_option(int option, int64_t value);
+ONYX_API int64_t onyx_get_option(int option);
+
+/*
  * Masked greedy selection over `rows` rows of `vocab` logits.
  * Replaces TorchCUDAGrammarLogitMask.apply + select_cuda_argmax for a whole batch
  * (onyx_cuda/src/onyx_cuda/torch_grammar_mask.py:69-86 and torch_backend.py:970-1007).

@@ -26,6 +26,13 @@ ERR_CUDA = 4
 ERR_SCRATCH_LIMIT = 5
 NOALLOC_SCRATCH_BYTES = 1 << 20
 
+OPTION_CLUSTER = 0
+OPTION_PDL = 1
+OPTION_STREAM = 2
+OPTION_SAMPLE_FORM = 3
+OPTION_TEST_WITHHELD_KEY_BYTES = 4
+STREAM_NEVER, STREAM_ALWAYS, STREAM_AUTO = 0, 1, 2
+
 STATUS_EMPTY_MASK = 1
 STATUS_ALL_NEG_INF = 2
 STATUS_NAN_IN_SUPPORT = 4
@@ -38,6 +45,8 @@ SIGNATURES: dict[str, tuple[object, list]] = {
     "onyx_abi_version": (_i32, []),
     "onyx_error_string": (ctypes.c_char_p, [_i32]),
     "onyx_last_cuda_error": (_i32, []),
+    "onyx_set_option": (_i32, [_i32, _i64]),
+    "onyx_get_option": (_i64, [_i32]),
     "onyx_masked_argmax_workspace_size": (_sz, [_i64, _i64, _i32]),
     "onyx_masked_argmax": (
         _i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _sz, _vp]),
@@ -135,3 +144,32 @@ def check(function: str, code: int) -> None:
     if code == ERR_CUDA:
         message += f"; cudaError {lib.onyx_last_cuda_error()}"
     raise OnyxCallError(function, code, message)
+
+
+def set_option(option: int, value: int) -> None:
+    """Set a process-wide library option (``OPTION_*``; diagnostic and test switches)."""
+    check("onyx_set_option", load().onyx_set_option(int(option), int(value)))
+
+
+def get_option(option: int) -> int:
+    return int(load().onyx_get_option(int(option)))
+
+
+class option_override:
+    """Context manager: set library options for the duration of a block, then restore them.
+
+    ``with option_override({OPTION_STREAM: STREAM_NEVER}): ...``"""
+
+    def __init__(self, values: dict[int, int]) -> None:
+        self.values = dict(values)
+        self.saved: dict[int, int] = {}
+
+    def __enter__(self):
+        for k, v in self.values.items():
+            self.saved[k] = get_option(k)
+            set_option(k, v)
+        return self
+
+    def __exit__(self, *exc):
+        for k, v in self.saved.items():
+            set_option(k, v)

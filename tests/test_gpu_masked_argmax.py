@@ -8,6 +8,7 @@ import pytest
 import torch
 
 import oracle
+from onyx_b200 import _lib
 from onyx_b200 import masked_selection as ms
 from onyx_b200 import workloads
 from oracle.regex_dfa import compile_regex_dfa
@@ -219,12 +220,24 @@ def test_workspace_is_left_zeroed_across_layouts(cuda_lib):
             assert int(torch.count_nonzero(buf)) == 0
 
 
-@pytest.mark.parametrize("path", ["cluster", "ticket"])
-def test_both_cross_cta_combines_match_oracle(path, monkeypatch, cuda_lib):
+PATHS = {
+    "cluster": {_lib.OPTION_STREAM: _lib.STREAM_NEVER, _lib.OPTION_CLUSTER: 1},
+    "ticket": {_lib.OPTION_STREAM: _lib.STREAM_NEVER, _lib.OPTION_CLUSTER: 0},
+    "stream": {_lib.OPTION_STREAM: _lib.STREAM_ALWAYS, _lib.OPTION_CLUSTER: 1},
+}
+
+
+@pytest.mark.parametrize("path", list(PATHS))
+def test_every_cross_cta_combine_matches_oracle(path, cuda_lib):
     """Rows that fit one thread-block cluster merge CTA partials through distributed shared
-    memory; ONYX_B200_CLUSTER=0 forces the global-ticket merge. Both must agree with the
-    oracle for argmax, gather and shard keys."""
-    monkeypatch.setenv("ONYX_B200_CLUSTER", "1" if path == "cluster" else "0")
+    memory; the CLUSTER option off forces the global-ticket merge; the STREAM option on
+    forces the streaming form (split rows merged by 128-bit compare-and-swap). All must
+    agree with the oracle for argmax, gather and shard keys."""
+    with _lib.option_override(PATHS[path]):
+        _combine_cases()
+
+
+def _combine_cases():
     w = workloads.batched(rows=16)
     x, m = to_device(w["logits_bf16"], "bf16"), masks_to_device(w["masks"])
     idx_ref, st_ref = oracle.masked_argmax(w["logits_bf16"], w["masks"], dtype="bf16")

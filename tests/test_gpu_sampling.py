@@ -14,6 +14,7 @@ import pytest
 import torch
 
 from oracle import sampling as osamp
+from onyx_b200 import _lib
 from onyx_b200 import masked_selection as ms
 from onyx_b200 import sampling, workloads
 from tests.conftest import golden_values, load_golden
@@ -22,17 +23,14 @@ from tests.gpu_util import host, masks_to_device, requires_cuda, to_device
 pytestmark = [pytest.mark.gpu, requires_cuda]
 
 # Kernel forms: the default (a cluster of CTAs per row, sized from the batch), the one-CTA
-# kernel, and clusters of 3 and 16 CTAs (ONYX_B200_SAMPLE_FORM, read at every call).
-FORMS = ["default", "single", "cluster:3", "cluster:16"]
+# kernel, and clusters of 3 and 16 CTAs (the library option ONYX_OPTION_SAMPLE_FORM).
+FORMS = {"default": 0, "single": -1, "cluster:3": 3, "cluster:16": 16}
 
 
-@pytest.fixture(params=FORMS)
-def form(request, monkeypatch):
-    if request.param == "default":
-        monkeypatch.delenv("ONYX_B200_SAMPLE_FORM", raising=False)
-    else:
-        monkeypatch.setenv("ONYX_B200_SAMPLE_FORM", request.param)
-    return request.param
+@pytest.fixture(params=list(FORMS))
+def form(request, cuda_lib):
+    with _lib.option_override({_lib.OPTION_SAMPLE_FORM: FORMS[request.param]}):
+        yield request.param
 
 
 def _float64(x: np.ndarray, dtype: str) -> np.ndarray:

@@ -1,7 +1,8 @@
 """The cluster path's one wait is bounded: rank 0 of a row's cluster waits on an mbarrier for
 the other CTAs' keys, and gives up after 0.5 s with ONYX_STATUS_WAIT_TIMEOUT instead of
-hanging. ONYX_B200_TEST_WITHHELD_KEY_BYTES makes rank 0 expect key bytes that no CTA sends,
-so the wait runs out; nothing faults, and the context stays usable afterwards."""
+hanging. The test option ONYX_OPTION_TEST_WITHHELD_KEY_BYTES makes rank 0 expect key bytes
+that no CTA sends, so the wait runs out; nothing faults, and the context stays usable
+afterwards."""
 
 from __future__ import annotations
 
@@ -12,6 +13,7 @@ import pytest
 import torch
 
 import oracle
+from onyx_b200 import _lib
 from onyx_b200 import masked_selection as ms
 from onyx_b200 import workloads
 from tests.gpu_util import host, masks_to_device, requires_cuda, to_device
@@ -26,10 +28,20 @@ def _inputs(rows, vocab=128256, seed=4):
     return x, m
 
 
-def test_withheld_keys_time_out_and_the_context_recovers(monkeypatch, cuda_lib):
+def test_withheld_keys_time_out_and_the_context_recovers(cuda_lib):
     x, m = _inputs(2)
     xd, md = to_device(x, "bf16"), masks_to_device(m)
-    monkeypatch.setenv("ONYX_B200_TEST_WITHHELD_KEY_BYTES", "8")
+    with _lib.option_override({_lib.OPTION_STREAM: _lib.STREAM_NEVER, _lib.OPTION_CLUSTER: 1,
+                               _lib.OPTION_TEST_WITHHELD_KEY_BYTES: 8}):
+        _withheld_calls(xd, md)
+
+    idx_ref, st_ref = oracle.masked_argmax(x, m, dtype="bf16")
+    r2 = ms.masked_argmax(xd, md)
+    np.testing.assert_array_equal(host(r2.token_ids).astype(np.int64), idx_ref.astype(np.int64))
+    np.testing.assert_array_equal(host(r2.status).astype(np.int64), st_ref.astype(np.int64))
+
+
+def _withheld_calls(xd, md):
     t0 = time.perf_counter()
     r = ms.masked_argmax(xd, md)
     torch.cuda.synchronize()
@@ -48,9 +60,3 @@ def test_withheld_keys_time_out_and_the_context_recovers(monkeypatch, cuda_lib):
     keys = ms.vocab_partial_keys(xd, md, 0)
     c = ms.combine_partial_keys(keys[None])
     assert list(host(c.status)) == [ms.STATUS_WAIT_TIMEOUT] * 2
-
-    monkeypatch.delenv("ONYX_B200_TEST_WITHHELD_KEY_BYTES")
-    idx_ref, st_ref = oracle.masked_argmax(x, m, dtype="bf16")
-    r2 = ms.masked_argmax(xd, md)
-    np.testing.assert_array_equal(host(r2.token_ids).astype(np.int64), idx_ref.astype(np.int64))
-    np.testing.assert_array_equal(host(r2.status).astype(np.int64), st_ref.astype(np.int64))
