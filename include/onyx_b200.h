@@ -261,16 +261,21 @@ ONYX_API int onyx_vocab_exchange_argmax(const void* logits, int dtype, int64_t r
  * code where an allocation would synchronise or fail -- and so cannot pass a workspace.
  * The caller passes only inputs and outputs (same meaning as onyx_masked_argmax).
  *
- * The partials and tickets of rows split over several CTAs live in a fixed scratch array
- * compiled into the library: ONYX_NOALLOC_SCRATCH_BYTES (1 MiB) held on every GPU that
- * loads the library until the process exits. A request needing more than that --
- * 4 bytes per row plus 16 bytes per row per 16,384 16-bit (8,192 f32) columns, rounded
- * up -- returns ONYX_ERR_SCRATCH_LIMIT without launching anything. The call allocates nothing: the first
- * call on each device looks up the scratch address (cudaGetSymbolAddress, on the current
- * device), so make that first call before any stream capture; every call clears the
- * tickets it uses with cudaMemsetAsync on `stream`. All calls on a device share the one
- * array, so calls that can overlap on the GPU (other streams or host threads) race and
- * must be serialised by the caller.
+ * Rows that fit one thread-block cluster (up to 8 x 16 warp segments: 262,144 columns of a
+ * 16-byte aligned 16-bit row, 131,072 of f32, 131,072 of an unaligned row) combine inside
+ * the cluster and use no scratch, unless ONYX_OPTION_CLUSTER is off. Longer rows, and f64
+ * rows, keep their partials and tickets in a fixed scratch array compiled into the
+ * library: ONYX_NOALLOC_SCRATCH_BYTES (1 MiB) held on every GPU that loads the library
+ * until the process exits. Such a request needs 4 bytes per row (rounded up to 256) plus
+ * 16 bytes per row per CTA; a CTA covers 16,384 columns of a 16-byte aligned 16-bit row,
+ * 8,192 columns of an aligned f32 row, and 8,192 columns otherwise (unaligned rows, f64).
+ * A request needing more returns ONYX_ERR_SCRATCH_LIMIT without launching anything. The
+ * call allocates nothing: the first call that needs the scratch in a CUDA context looks up
+ * its address (cudaGetSymbolAddress) and keeps it for that context, so make that first call
+ * (for the primary context, the first on each device) before any stream capture; every
+ * call that uses the scratch clears its tickets with cudaMemsetAsync on `stream`. All calls
+ * in a context share the one array, so calls that can overlap on the GPU (other streams or
+ * host threads) race and must be serialised by the caller.
  */
 ONYX_API int onyx_masked_argmax_noalloc(const void* logits, int dtype, int64_t rows,
                                         int64_t vocab, int64_t row_stride, const uint32_t* mask,

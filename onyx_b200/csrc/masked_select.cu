@@ -26,6 +26,8 @@
 #include "onyx_common.cuh"
 #include "../../include/onyx_b200.h"
 
+#include <cuda.h>  // CUcontext / CUresult only: the driver entry point is looked up at run time
+
 
 #include <algorithm>
 #include <atomic>
@@ -84,6 +86,7 @@ struct ScanParams {
   int n_key_dst;
   int64_t key_parity_stride;
   const unsigned long long* key_epoch;
+  const unsigned long long* key_failed;  // nonzero: the exchange failed, store no key
 };
 
 constexpr int kMaxPerGroup = 256;
@@ -520,8 +523,11 @@ __device__ __forceinline__ void finalize_group(const ScanParams& p, int64_t grou
       if (r.flags & kFlagAny) key = (r.ord << 32) | (unsigned long long)(0xFFFFFFFFu - r.idx);
       if (r.flags & kFlagWaitTimeout) key = kKeyWaitTimeout;
       if (p.n_key_dst) {
-        const int64_t slot = ((__ldcg(p.key_epoch) + 1ull) & 1ull ? p.key_parity_stride : 0) + group;
-        for (int i = 0; i < p.n_key_dst; ++i) p.key_dst[i][slot] = key;
+        if (__ldcg(p.key_failed) == 0ull) {
+          const int64_t slot =
+              ((__ldcg(p.key_epoch) + 1ull) & 1ull ? p.key_parity_stride : 0) + group;
+          for (int i = 0; i < p.n_key_dst; ++i) p.key_dst[i][slot] = key;
+        }
       } else {
         p.out_key[group] = key;
       }
@@ -728,14 +734,16 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* bar, u
                : "memory");
 }
 
+// The waiting warp is parked by the hardware until the phase completes or the hint (ns)
+// passes, instead of polling.
 __device__ __forceinline__ bool mbar_try_wait_cluster(unsigned long long* bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(1000000u)
       : "memory");
   return done != 0u;
 }
@@ -2086,6 +2094,7 @@ int onyx_vocab_exchange_argmax(const void* logits, int dtype, int64_t rows, int6
   p.n_key_dst = world;
   p.key_parity_stride = (int64_t)world * rows_cap;
   p.key_epoch = own_epoch;
+  p.key_failed = reinterpret_cast<unsigned long long*>(own + kExchangeFailedOffset);
   ExchangeParams x = {};
   for (int i = 0; i < world; ++i) {
     char* base = static_cast<char*>(exchange_bases[i]);
@@ -2095,6 +2104,7 @@ int onyx_vocab_exchange_argmax(const void* logits, int dtype, int64_t rows, int6
   }
   x.own_flags = reinterpret_cast<unsigned long long*>(own);
   x.own_epoch = own_epoch;
+  x.own_failed = reinterpret_cast<unsigned long long*>(own + kExchangeFailedOffset);
   x.slots = reinterpret_cast<const unsigned long long*>(own + kExchangeFlagBytes);
   x.parity_stride = (int64_t)world * rows_cap;
   x.world = world;
@@ -2226,47 +2236,78 @@ int onyx_combine_partials(const uint64_t* keys, int64_t n_parts, int64_t rows, i
 // so cannot hand over a workspace -- e.g. a serving process whose device memory was
 // reserved up front by its own pool, a host-language binding that only ever receives
 // pointers to buffers someone else allocated, or code running where an allocation would
-// synchronise or fail. This entry point takes only inputs and outputs; the split-row
-// partials and tickets live in a fixed scratch array compiled into the library.
+// synchronise or fail. This entry point takes only inputs and outputs. Rows that fit one
+// thread-block cluster need no scratch at all (their CTAs combine in distributed shared
+// memory); longer rows, or every row when the cluster option is off, keep their split-row
+// partials and tickets in a fixed scratch array compiled into the library.
 //
 // The array is a file-scope __device__ symbol, so every GPU that loads this library holds
 // kNoAllocScratchBytes of it until the process exits. Host code cannot use the symbol's
-// name as a device address; the address is looked up once per device with
-// cudaGetSymbolAddress, with that device current, on the first call made on that device.
-// That first call should therefore happen before any stream capture. Every call on a
-// device shares the one array: calls whose kernels may overlap on the GPU (different
-// streams, or different host threads) race and must be serialised by the caller.
+// name as a device address: the address is looked up with cudaGetSymbolAddress in each
+// CUDA context, by the first call that needs the scratch in that context (for the usual
+// primary context, the first such call on each device), and kept per context. That first
+// call should therefore happen before any stream capture. Every call in a context shares
+// the one array: calls whose kernels may overlap on the GPU (different streams, or
+// different host threads) race and must be serialised by the caller.
 // ---------------------------------------------------------------------------------------
 namespace onyx {
 
 constexpr size_t kNoAllocScratchBytes = ONYX_NOALLOC_SCRATCH_BYTES;  // 1 MiB per device
-constexpr int kNoAllocMaxDevices = 64;
+constexpr int kNoAllocMaxContexts = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-static std::mutex g_noalloc_mutex;
-static void* g_noalloc_address[kNoAllocMaxDevices] = {};
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
 
-// Device address of this device's scratch array (looked up on first use).
+// The calling thread's current driver context, nullptr if there is none (the driver entry
+// point is looked up at run time, so the library does not link the driver library).
+static CUcontext current_context() {
+  static const CtxGetCurrentFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      (void)cudaGetLastError();
+      f = nullptr;
+    }
+    return reinterpret_cast<CtxGetCurrentFn>(f);
+  }();
+  CUcontext c = nullptr;
+  if (!fn || fn(&c) != CUDA_SUCCESS) return nullptr;
+  return c;
+}
+
+struct NoAllocEntry {
+  CUcontext ctx;
+  void* ptr;
+};
+static std::mutex g_noalloc_mutex;
+static NoAllocEntry g_noalloc_cache[kNoAllocMaxContexts] = {};
+static int g_noalloc_next = 0;
+
+// Device address of the scratch array in the current context (looked up on first use).
 static int noalloc_scratch_address(void** out) {
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) {
-    g_last_cuda_error = (int)e;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  CUcontext ctx = current_context();
+  if (ctx) {
+    for (const NoAllocEntry& en : g_noalloc_cache)
+      if (en.ctx == ctx && en.ptr) {
+        *out = en.ptr;
+        return ONYX_OK;
+      }
+  }
+  void* ptr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);  // makes a context current
+  if (e != cudaSuccess || ptr == nullptr) {
+    g_last_cuda_error = (int)(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
     return ONYX_ERR_CUDA;
   }
-  if (dev < 0 || dev >= kNoAllocMaxDevices) return ONYX_ERR_INVALID_ARGUMENT;
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!g_noalloc_address[dev]) {
-    void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess || ptr == nullptr) {
-      g_last_cuda_error = (int)(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
-      return ONYX_ERR_CUDA;
-    }
-    g_noalloc_address[dev] = ptr;
+  if (!ctx) ctx = current_context();
+  if (ctx) {
+    g_noalloc_cache[g_noalloc_next] = NoAllocEntry{ctx, ptr};
+    g_noalloc_next = (g_noalloc_next + 1) % kNoAllocMaxContexts;
   }
-  *out = g_noalloc_address[dev];
+  *out = ptr;
   return ONYX_OK;
 }
 
@@ -2285,11 +2326,6 @@ extern "C" int onyx_masked_argmax_noalloc(const void* logits, int dtype, int64_t
   const int es = dtype_bytes(dtype);
   const bool aligned = aligned16(logits) && ((row_stride * es) % 16 == 0 || rows == 1);
   const Plan pl = make_plan(dtype, vocab, aligned);
-  // scratch layout: ticket counters [rows] first, then partials [rows * segs]
-  const size_t count_bytes = align_up((size_t)rows * sizeof(uint32_t), 256);
-  const size_t part_bytes = (size_t)rows * pl.ctas_per_row * sizeof(Partial);
-  const bool split = pl.ctas_per_row > 1;
-  if (split && count_bytes + part_bytes > kNoAllocScratchBytes) return ONYX_ERR_SCRATCH_LIMIT;
   ScanParams p = {};
   p.logits = logits;
   p.group_stride = row_stride;
@@ -2303,6 +2339,16 @@ extern "C" int onyx_masked_argmax_noalloc(const void* logits, int dtype, int64_t
   p.seg_elems = pl.seg_elems;
   p.out_idx = out_idx;
   p.out_status = out_status;
+  // rows that fit one cluster: no scratch
+  cudaError_t cluster_err = cudaSuccess;
+  if (dispatch_cluster<kModeArgmax>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled(),
+                                    &cluster_err))
+    return finish_launch(cluster_err);
+  // scratch layout: ticket counters [rows] first, then partials [rows * ctas_per_row]
+  const size_t count_bytes = align_up((size_t)rows * sizeof(uint32_t), 256);
+  const size_t part_bytes = (size_t)rows * pl.ctas_per_row * sizeof(Partial);
+  const bool split = pl.ctas_per_row > 1;
+  if (split && count_bytes + part_bytes > kNoAllocScratchBytes) return ONYX_ERR_SCRATCH_LIMIT;
   if (split) {
     void* base = nullptr;
     rc = noalloc_scratch_address(&base);

@@ -24,9 +24,10 @@
 //   one CTA's range is final there; a row split over CTAs is merged through a 16-byte slot
 //   in the caller's workspace {key, contributors so far} with a 128-bit compare-and-swap:
 //   the CTA whose swap completes the count holds the row's key and writes the outputs, and
-//   resets the slot to zero. Verify joins the rows of one batch entry the same way: a 16-byte slot per
-//   entry holds the miss bits, the count, and the deciding row's selection, so the entry's
-//   last row decides from its own swap result. No thread waits on another CTA.
+//   resets the slot to zero. Verify joins the rows of one batch entry the same way: a
+//   16-byte slot per entry holds the miss bits, the count, and the deciding row's
+//   selection, so the entry's last row decides from its own swap result. No thread waits
+//   on another CTA.
 // * Every wait (a stage filling, a stage being released) is bounded by %globaltimer; a CTA
 //   that gives up stops waiting altogether, marks its rows ONYX_STATUS_WAIT_TIMEOUT, and its
 //   producer waits (bounded) for the copies it issued before the CTA exits.
@@ -59,14 +60,19 @@ __device__ __forceinline__ void mbar_arrive_cta(unsigned long long* bar) {
                : "memory");
 }
 
+// Suspend-time hint of a try_wait: a waiting warp is parked by the hardware until the phase
+// completes or this many nanoseconds pass, so waiting costs no issue slots (a plain
+// try_wait returns after a short system limit and turns the wait into a polling loop).
+constexpr uint32_t kStreamSuspendNs = 1000000u;  // 1 ms
+
 __device__ __forceinline__ bool mbar_try_wait_cta(unsigned long long* bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(kStreamSuspendNs)
       : "memory");
   return done != 0u;
 }
@@ -232,8 +238,10 @@ __device__ void stream_emit_final(const ScanParams& p, int64_t r, unsigned long 
     decode_partial(pr, false, &p.out_idx[r], &p.out_status[r]);
   } else if constexpr (MODE == kModeKey) {
     if (p.n_key_dst) {
-      const int64_t slot = ((__ldcg(p.key_epoch) + 1ull) & 1ull ? p.key_parity_stride : 0) + r;
-      for (int i = 0; i < p.n_key_dst; ++i) p.key_dst[i][slot] = key;
+      if (__ldcg(p.key_failed) == 0ull) {  // a failed exchange stores no key anywhere
+        const int64_t slot = ((__ldcg(p.key_epoch) + 1ull) & 1ull ? p.key_parity_stride : 0) + r;
+        for (int i = 0; i < p.n_key_dst; ++i) p.key_dst[i][slot] = key;
+      }
     } else {
       p.out_key[r] = key;
     }

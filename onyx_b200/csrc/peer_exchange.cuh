@@ -4,7 +4,8 @@
 // Every rank owns one exchange buffer, allocated with cudaMalloc and mapped into every
 // other rank's address space through CUDA IPC:
 //
-//   [flags: kMaxExchangeRanks x u64 | epoch count: u64 at byte 128 | ... 256 bytes]
+//   [flags: kMaxExchangeRanks x u64 | epoch count: u64 at byte 128 | failed: u64 at byte
+//    136 | ... 256 bytes]
 //   [slots: 2 parities x world x rows_cap x u64]
 //
 // The epoch count is this rank's number of finished calls; call e is the count + 1, read on
@@ -20,15 +21,24 @@
 // rank raises after its own call e - 1 finished reading; with two parities no store can
 // land in a slot a peer is still reading. Flags only grow, so a rank that has moved on
 // to e + 1 never hides e from a slower peer.
+//
+// A wait that gives up breaks that invariant (this rank no longer knows which slots its
+// peers read), so the failure is sticky: the exchange kernel sets this rank's "failed"
+// word and leaves the epoch count where it was; from then on the shard kernel stores no
+// key into any buffer and the exchange kernel neither raises flags nor waits -- every row
+// of every later call reports ONYX_STATUS_WAIT_TIMEOUT until the ranks build new buffers.
+// Peers waiting on this rank's flag give up in turn and fail the same way.
 
 constexpr int kMaxExchangeRanks = 8;
 constexpr size_t kExchangeFlagBytes = 256;
 constexpr size_t kExchangeEpochOffset = 128;  // this rank's count of finished calls
+constexpr size_t kExchangeFailedOffset = 136;  // nonzero once a wait of this rank gave up
 constexpr unsigned long long kExchangeWaitLimitNs = 2000ull * 1000ull * 1000ull;  // 2 s
 
 struct ExchangeParams {
   unsigned long long* own_flags;               // this rank's buffer: one flag per rank
   unsigned long long* own_epoch;               // this rank's buffer: finished calls
+  unsigned long long* own_failed;              // this rank's buffer: sticky failure
   unsigned long long* flag_dst[kMaxExchangeRanks];  // this rank's flag in every rank's buffer
   const unsigned long long* slots;             // this rank's buffer, parity 0
   int64_t parity_stride;                       // world * rows_cap
@@ -57,15 +67,18 @@ __global__ void __launch_bounds__(1024) exchange_combine_kernel(const ExchangePa
   if (threadIdx.x == 0) {
     const unsigned long long epoch = __ldcg(e.own_epoch) + 1ull;
     s_epoch = epoch;
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-    for (int i = 0; i < e.world; ++i) st_release_sys_u64(e.flag_dst[i], epoch);
-    bool ok = true;
-    const unsigned long long t0 = global_ns();
-    for (int i = 0; i < e.world && ok; ++i) {
-      while (ld_acquire_sys_u64(e.own_flags + i) < epoch) {
-        if (global_ns() - t0 > kExchangeWaitLimitNs) {
-          ok = false;
-          break;
+    bool ok = __ldcg(e.own_failed) == 0ull;
+    if (ok) {
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      for (int i = 0; i < e.world; ++i) st_release_sys_u64(e.flag_dst[i], epoch);
+      const unsigned long long t0 = global_ns();
+      for (int i = 0; i < e.world && ok; ++i) {
+        while (ld_acquire_sys_u64(e.own_flags + i) < epoch) {
+          if (global_ns() - t0 > kExchangeWaitLimitNs) {
+            ok = false;
+            __stcg(e.own_failed, 1ull);  // sticky: later calls neither store nor wait
+            break;
+          }
         }
       }
     }
@@ -87,5 +100,6 @@ __global__ void __launch_bounds__(1024) exchange_combine_kernel(const ExchangePa
     pr.idx = 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull);
     decode_partial(pr, false, &e.out_idx[r], &e.out_status[r]);
   }
-  if (threadIdx.x == 0) __stcg(e.own_epoch, s_epoch);  // the next call's shard kernel reads it
+  // the next call's shard kernel reads the count for its parity; a failed exchange keeps it
+  if (threadIdx.x == 0 && ok) __stcg(e.own_epoch, s_epoch);
 }

@@ -148,6 +148,49 @@ def test_peer_exchange_single_rank_matches_oracle(cuda_lib):
         assert lib.onyx_ipc_free(own.value) == _lib.OK
 
 
+def test_peer_exchange_wait_times_out_and_stays_failed(cuda_lib):
+    """A peer whose flag never rises: rank 0 of a two-rank world whose second buffer is a
+    zero-filled local allocation that no kernel ever raises. The exchange kernel's bounded
+    wait (2 s) gives up and every row reports WAIT_TIMEOUT; the failure is sticky, so the
+    next call reports it at once and stores no key into the other buffer. Nothing faults or
+    hangs: one kernel waits, for a flag nothing sets, and gives up."""
+    import ctypes
+    import time
+
+    from onyx_b200 import _lib
+    lib = cuda_lib
+    rows, rows_cap, world = 16, 16, 2
+    nbytes = lib.onyx_exchange_buffer_bytes(world, rows_cap)
+    handle = ctypes.create_string_buffer(lib.onyx_ipc_handle_bytes())
+    own = ctypes.c_void_p()
+    assert lib.onyx_ipc_alloc(nbytes, ctypes.byref(own), handle) == _lib.OK
+    peer = torch.zeros(nbytes, dtype=torch.uint8, device="cuda:0")
+    bases = (ctypes.c_void_p * world)(own.value, peer.data_ptr())
+    w = workloads.scaling(seed=9, rows=rows, vocab=32000)
+    lo, hi = vocab_parallel.vocab_shard_bounds(32000, 0, world)
+    xt = to_device(np.ascontiguousarray(w["logits_bf16"][:, lo:hi]), "bf16")
+    mt = masks_to_device(np.ascontiguousarray(w["masks"][:, lo // 32:hi // 32]))
+    try:
+        t0 = time.perf_counter()
+        res = ms.vocab_exchange_argmax(xt, mt, lo, world=world, rank=0, exchange_bases=bases,
+                                       rows_cap=rows_cap)
+        torch.cuda.synchronize()
+        assert time.perf_counter() - t0 > 1.5  # the bounded wait ran out
+        assert list(host(res.status)) == [ms.STATUS_WAIT_TIMEOUT] * rows
+        assert list(host(res.token_ids)) == [-1] * rows
+        peer.zero_()
+        t0 = time.perf_counter()
+        res2 = ms.vocab_exchange_argmax(xt, mt, lo, world=world, rank=0, exchange_bases=bases,
+                                        rows_cap=rows_cap)
+        torch.cuda.synchronize()
+        assert time.perf_counter() - t0 < 1.0  # failed already: no second wait
+        assert list(host(res2.status)) == [ms.STATUS_WAIT_TIMEOUT] * rows
+        assert int(torch.count_nonzero(peer)) == 0  # neither keys nor flags were stored
+    finally:
+        torch.cuda.synchronize()
+        assert lib.onyx_ipc_free(own.value) == _lib.OK
+
+
 def test_peer_exchange_rejects_bad_arguments(cuda_lib):
     import ctypes
     from onyx_b200 import _lib

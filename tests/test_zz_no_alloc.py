@@ -49,18 +49,36 @@ def _without_workspace(lib, x, m):
     return idx, st
 
 
-def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(cuda_lib):
+@pytest.mark.parametrize("cluster", [1, 0], ids=["cluster-combine", "scratch-combine"])
+def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(cluster, cuda_lib):
+    """With the cluster option on, rows that fit one cluster combine in distributed shared
+    memory and the scratch is not touched; with it off, every split row goes through the
+    fixed scratch array. Both must match the workspace entry point, call after call."""
     lib = cuda_lib
     first = workloads.batched()  # 64 x 128,256 bf16: rows split over 63 warps each
     second = workloads.batched(seed=77, rows=40, vocab=151936)
-    for w in (first, second, first):
-        x = to_device(w["logits_bf16"], "bf16")
-        m = masks_to_device(w["masks"])
-        ref_idx, ref_st = _with_workspace(lib, x, m)
-        got_idx, got_st = _without_workspace(lib, x, m)
+    with _lib.option_override({_lib.OPTION_CLUSTER: cluster}):
+        for w in (first, second, first):
+            x = to_device(w["logits_bf16"], "bf16")
+            m = masks_to_device(w["masks"])
+            ref_idx, ref_st = _with_workspace(lib, x, m)
+            got_idx, got_st = _without_workspace(lib, x, m)
+            torch.cuda.synchronize()
+            assert torch.equal(got_idx, ref_idx)
+            assert torch.equal(got_st, ref_st)
+
+
+def test_noalloc_rows_longer_than_a_cluster_use_the_scratch(cuda_lib):
+    """300,000-column rows need 147 warp segments, more than one cluster holds: their CTAs
+    combine through the fixed scratch even with the cluster option on."""
+    w = workloads.batched(seed=5, rows=6, vocab=300000)
+    x = to_device(w["logits_bf16"], "bf16")
+    m = masks_to_device(w["masks"])
+    for _ in range(2):
+        ref_idx, ref_st = _with_workspace(cuda_lib, x, m)
+        got_idx, got_st = _without_workspace(cuda_lib, x, m)
         torch.cuda.synchronize()
-        assert torch.equal(got_idx, ref_idx)
-        assert torch.equal(got_st, ref_st)
+        assert torch.equal(got_idx, ref_idx) and torch.equal(got_st, ref_st)
 
 
 def test_noalloc_unmasked_rows(cuda_lib):
@@ -75,10 +93,14 @@ def test_noalloc_unmasked_rows(cuda_lib):
 
 
 def test_noalloc_rejects_requests_beyond_its_scratch(cuda_lib):
-    """A request whose split-row partials exceed the fixed scratch is refused before any
-    launch. The buffers are real and sized for the request, so nothing could read out of
-    bounds even if the call were accepted."""
-    lib = cuda_lib
+    """With the cluster option off, a request whose split-row partials exceed the fixed
+    scratch is refused before any launch. The buffers are real and sized for the request,
+    so nothing could read out of bounds even if the call were accepted."""
+    with _lib.option_override({_lib.OPTION_CLUSTER: 0}):
+        _rejects_beyond_scratch(cuda_lib)
+
+
+def _rejects_beyond_scratch(lib):
     rows, vocab = 32768, 16385  # 9 warp segments -> 2 CTAs per row: 32,768 * (4 + 32) B > 1 MiB
     count_bytes = (rows * 4 + 255) // 256 * 256
     assert count_bytes + rows * 2 * 16 > _lib.NOALLOC_SCRATCH_BYTES
