@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this folder from the reference's own Python code.
 
-Run once in a container that holds the reference checkout (read-only) at
-``/root/reference``; the outputs are committed and the tests only read the JSON files.
+Run once where a checkout of the reference (read-only) is available, passing its root
+directory; the outputs are committed and the tests only read the JSON files.
 
 * ``regex_parity.json`` -- the reference's frozen regex outcomes
   (onyx_cuda/tests/regex_parity_fixtures.py:22-104, imported as data) plus the vectors
@@ -23,8 +23,13 @@ Run once in a container that holds the reference checkout (read-only) at
   ``decide_grammar_masked_post_acceptance_continuation`` (grammar_continuation.py:102)
   driving a scripted ``FakeGrammarConstraint`` (testing.py:715) whose per-position
   valid sets are the case's bitmasks.
+* ``iteration_cases.json`` -- the same pair of reference functions driving a branching
+  scripted grammar (tokens lead to different states, some states admit nothing, some
+  match), recording both result objects in full: accepted count, replacement, the
+  no-decision selections, the committed states (by name) and match facts, the output
+  tokens, and how many grammar states are still alive afterwards.
 
-Usage:  python tests/golden/make_golden.py
+Usage:  python tests/golden/make_golden.py <reference checkout root>
 """
 
 from __future__ import annotations
@@ -37,7 +42,9 @@ from pathlib import Path
 
 import numpy as np
 
-REFERENCE = Path("/root/reference")
+if len(sys.argv) != 2 or not (Path(sys.argv[1]) / "onyx_cuda" / "src").is_dir():
+    raise SystemExit("usage: python tests/golden/make_golden.py <reference checkout root>")
+REFERENCE = Path(sys.argv[1])
 sys.path.insert(0, str(REFERENCE / "onyx_cuda" / "src"))
 sys.path.insert(0, str(REFERENCE / "onyx_cuda" / "tests"))
 
@@ -391,6 +398,98 @@ def verify_fixtures(rng: np.random.Generator) -> dict:
     return {"cases": cases}
 
 
+# ---------------------------------------------------------------------------
+# whole speculative iterations (acceptance + continuation) on a branching grammar
+# ---------------------------------------------------------------------------
+def _branching_constraint(rng: np.random.Generator, vocab_size: int, n_states: int):
+    """Scripted grammar of n_states states: each admits a random set of ids (some none),
+    each admitted id leads to a random state, some states match."""
+    names = [f"q{i}" for i in range(n_states)]
+    valid, transitions = [], []
+    for name in names:
+        if rng.random() < 0.12:
+            ids = []
+        else:
+            density = float(rng.uniform(0.05, 0.6))
+            ids = [j for j in range(vocab_size) if rng.random() < density] or [int(rng.integers(0, vocab_size))]
+        valid.append((name, tuple(ids)))
+        for t in ids:
+            transitions.append((name, t, names[int(rng.integers(0, n_states))]))
+    # a state that admits nothing must be a match state (the fake's own rule)
+    match_states = frozenset(n for (n, ids) in valid if not ids or rng.random() < 0.3)
+    program = FakeGrammarProgram(initial_state="q0", transitions=tuple(transitions),
+                                 valid_token_ids=tuple(valid), match_states=match_states)
+    vocabulary = tuple(f"t{i}".encode() for i in range(vocab_size))
+    return FakeGrammarConstraint(vocabulary, grammar_type="regex", program=program), program
+
+
+def _state_name(constraint, handle):
+    return None if handle is None else constraint._states[handle.value]
+
+
+def iteration_fixtures(rng: np.random.Generator) -> dict:
+    cases = []
+    for k in range(60):
+        gamma = int(rng.integers(1, 6))
+        v = int(rng.integers(8, 96))
+        n_states = int(rng.integers(3, 9))
+        constraint, program = _branching_constraint(rng, v, n_states)
+        valid_of = dict(program.valid_token_ids)
+        step_of = {(s, t): d for s, t, d in program.transitions}
+        start = constraint.init_state()
+        # rows of exactly representable f32 values; drafts follow the masked argmax along
+        # the grammar 70% of the time, so proposals are often accepted in full
+        rows = [[float(np.float32(x)) for x in rng.normal(0.0, 3.0, size=v)] for _ in range(gamma + 1)]
+        drafts, state = [], "q0"
+        for i in range(gamma):
+            ids = valid_of.get(state, ())
+            if ids and rng.random() < 0.75:
+                best = select_highest_logit(_list_mask(rows[i], set(ids)))
+                t = best if rng.random() < 0.8 else int(rng.choice(ids))
+            else:
+                t = int(rng.integers(0, v))
+            drafts.append(t)
+            state = step_of.get((state, t), state)
+        mask = _ListMask(v)
+        acceptance = decide_grammar_masked_target_acceptance(
+            tuple(drafts), tuple(tuple(r) for r in rows), constraint, start, mask,
+            vocab_size=v, select_token=select_highest_logit)
+        nd = acceptance.no_decision_selection
+        case = {
+            "name": f"iteration_{k}_g{gamma}_v{v}_s{n_states}",
+            "vocab_size": v,
+            "gamma": gamma,
+            "states": [[name, list(ids)] for name, ids in program.valid_token_ids],
+            "transitions": [[s, t, d] for s, t, d in program.transitions],
+            "match_states": sorted(program.match_states),
+            "rows_f32": rows,
+            "drafts": drafts,
+            "accepted_count": acceptance.accepted_count,
+            "replacement_token_id": acceptance.replacement_token_id,
+            "no_decision_is_match": None if nd is None else nd.is_match,
+            "acceptance_state": _state_name(constraint, acceptance.committed_state),
+            "acceptance_is_match": acceptance.committed_state_is_match,
+            "continuation": None,
+        }
+        if acceptance.decision_made:
+            state_name = _state_name(constraint, acceptance.committed_state)
+            cont = decide_grammar_masked_post_acceptance_continuation(
+                tuple(drafts), tuple(tuple(r) for r in rows), acceptance, constraint, mask,
+                vocab_size=v, select_token=select_highest_logit)
+            fr = cont.final_row_no_decision_selection
+            case["acceptance_state"] = state_name
+            case["continuation"] = {
+                "output_token_ids": list(cont.output_token_ids),
+                "uncached_next_token_id": cont.uncached_next_token_id,
+                "final_row_no_decision_is_match": None if fr is None else fr.is_match,
+                "committed_state": _state_name(constraint, cont.committed_state),
+                "committed_is_match": cont.committed_state_is_match,
+            }
+        case["active_states_after"] = constraint.active_state_count
+        cases.append(case)
+    return {"cases": cases}
+
+
 def _reference_kept(row_values: list[float], valid: list[int], temperature: float,
                     top_p: float):
     if not valid:
@@ -454,6 +553,7 @@ def main() -> None:
         "selection_cases.json": selection_fixtures(rng),
         "verify_cases.json": verify_fixtures(rng),
         "sampling_cases.json": sampling_fixtures(rng),
+        "iteration_cases.json": iteration_fixtures(np.random.default_rng(20261202)),
     }
     for name, payload in files.items():
         payload["generator"] = "tests/golden/make_golden.py"
