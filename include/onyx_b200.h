@@ -83,10 +83,6 @@ ONYX_API int onyx_last_cuda_error(void);
  *   CLUSTER      1: rows that fit one thread-block cluster use the cluster kernel;
  *                0: the global-ticket merge instead (ONYX_B200_CLUSTER, default 1).
  *   PDL          1: launches allow programmatic dependent launch (ONYX_B200_PDL, default 1).
- *   STREAM       when the streaming form (one CTA per SM, shared-memory ring fed by bulk
- *                copies) selects: ONYX_STREAM_NEVER, ONYX_STREAM_ALWAYS (every shape it can
- *                serve), ONYX_STREAM_AUTO (batches of several waves; ONYX_B200_STREAM,
- *                default AUTO).
  *   SAMPLE_FORM  masked sampling: 0 the cluster form with the cluster size chosen from the
  *                batch, -1 the one-CTA form, k in [1, 16] clusters of k CTAs
  *                (ONYX_B200_SAMPLE_FORM: "single" or "cluster:<k>", default 0).
@@ -96,13 +92,9 @@ ONYX_API int onyx_last_cuda_error(void);
  */
 #define ONYX_OPTION_CLUSTER 0
 #define ONYX_OPTION_PDL 1
-#define ONYX_OPTION_STREAM 2
-#define ONYX_OPTION_SAMPLE_FORM 3
-#define ONYX_OPTION_TEST_WITHHELD_KEY_BYTES 4
-#define ONYX_OPTION_COUNT 5
-#define ONYX_STREAM_NEVER 0
-#define ONYX_STREAM_ALWAYS 1
-#define ONYX_STREAM_AUTO 2
+#define ONYX_OPTION_SAMPLE_FORM 2
+#define ONYX_OPTION_TEST_WITHHELD_KEY_BYTES 3
+#define ONYX_OPTION_COUNT 4
 ONYX_API int onyx_set_option(int option, int64_t value);
 ONYX_API int64_t onyx_get_option(int option);
 

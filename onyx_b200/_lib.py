@@ -28,10 +28,8 @@ NOALLOC_SCRATCH_BYTES = 1 << 20
 
 OPTION_CLUSTER = 0
 OPTION_PDL = 1
-OPTION_STREAM = 2
-OPTION_SAMPLE_FORM = 3
-OPTION_TEST_WITHHELD_KEY_BYTES = 4
-STREAM_NEVER, STREAM_ALWAYS, STREAM_AUTO = 0, 1, 2
+OPTION_SAMPLE_FORM = 2
+OPTION_TEST_WITHHELD_KEY_BYTES = 3
 
 STATUS_EMPTY_MASK = 1
 STATUS_ALL_NEG_INF = 2
@@ -158,7 +156,7 @@ def get_option(option: int) -> int:
 class option_override:
     """Context manager: set library options for the duration of a block, then restore them.
 
-    ``with option_override({OPTION_STREAM: STREAM_NEVER}): ...``"""
+    ``with option_override({OPTION_CLUSTER: 0}): ...``"""
 
     def __init__(self, values: dict[int, int]) -> None:
         self.values = dict(values)

@@ -61,10 +61,6 @@ struct ScanParams {
   int64_t seg_elems;   // elements per warp segment (multiple of 32)
   Partial* ws_part;    // [rows * ctas_per_row], one partial per CTA
   uint32_t* ws_count;  // [groups]
-  // streaming form: {key, contributors} per row split over CTAs, and per verify group
-  // {miss bits | count | deciding row and status, its selection}
-  ulonglong2* row_slots;    // [rows]
-  ulonglong2* group_slots;  // [groups]
   // outputs
   int32_t* out_idx;
   uint32_t* out_status;
@@ -1100,7 +1096,6 @@ __global__ void combine_keys_kernel(const unsigned long long* keys, int64_t n_pa
   decode_partial(pr, false, &out_idx[r], &out_status[r]);
 }
 
-#include "masked_stream.cuh"
 #include "peer_exchange.cuh"
 #include "dfa_masks.cuh"
 #include "masked_sample.cuh"
@@ -1211,7 +1206,6 @@ static Options& options() {
     for (auto& a : x->v) a.store(0);
     x->v[ONYX_OPTION_CLUSTER].store(env_int("ONYX_B200_CLUSTER", 1) != 0 ? 1 : 0);
     x->v[ONYX_OPTION_PDL].store(env_int("ONYX_B200_PDL", 1) != 0 ? 1 : 0);
-    x->v[ONYX_OPTION_STREAM].store(env_int("ONYX_B200_STREAM", ONYX_STREAM_AUTO));
     x->v[ONYX_OPTION_SAMPLE_FORM].store(env_sample_form());
     return x;
   }();
@@ -1332,112 +1326,6 @@ static int bind_workspace(ScanParams& p, void* ws, size_t ws_bytes, size_t need,
 
 static bool dtype_ok(int dt) { return dt == kF32 || dt == kF16 || dt == kBF16 || dt == kF64; }
 
-// ---- streaming form (masked_stream.cuh) ------------------------------------------------
-// Logits bytes per launch from which ONYX_STREAM_AUTO takes the streaming form: beyond
-// about two waves of the one-shot kernels (148 SMs x 4 CTAs x 32 KB in flight per wave).
-constexpr int64_t kStreamAutoMinBytes = 36ll << 20;
-
-// Workspace bytes of the streaming form: one 16-byte slot per row that can be split over
-// CTAs, then one per verify group.
-static size_t stream_workspace_bytes(int64_t rows, int64_t groups, int64_t vocab,
-                                     int per_group) {
-  const size_t row_bytes =
-      (vocab > kStreamUnit) ? align_up((size_t)rows * sizeof(ulonglong2), 256) : 0;
-  const size_t group_bytes =
-      per_group > 1 ? align_up((size_t)groups * sizeof(ulonglong2), 256) : 0;
-  return row_bytes + group_bytes;
-}
-
-template <int DT, int MODE>
-static cudaError_t launch_stream_t(const ScanParams& p, int ctas, cudaStream_t stream, bool pdl) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)ctas, 1, 1);
-  cfg.blockDim = dim3(kStreamThreads, 1, 1);
-  cfg.dynamicSmemBytes = sizeof(StreamSmem);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, masked_stream_kernel<DT, MODE>, p);
-}
-
-// SM count of the current device, and the streaming kernels' shared-memory opt-in, once per
-// device. 0 on failure.
-static int stream_device_sms() {
-  static std::mutex mu;
-  static int sms[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
-    (void)cudaGetLastError();
-    return 0;
-  }
-  std::lock_guard<std::mutex> lock(mu);
-  if (!sms[dev]) {
-    int n = 0;
-    cudaError_t e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    const int bytes = (int)sizeof(StreamSmem);
-    const void* fns[] = {
-        (const void*)masked_stream_kernel<kBF16, kModeArgmax>,
-        (const void*)masked_stream_kernel<kBF16, kModeKey>,
-        (const void*)masked_stream_kernel<kBF16, kModeVerify>,
-        (const void*)masked_stream_kernel<kF16, kModeArgmax>,
-        (const void*)masked_stream_kernel<kF16, kModeKey>,
-        (const void*)masked_stream_kernel<kF16, kModeVerify>,
-        (const void*)masked_stream_kernel<kF32, kModeArgmax>,
-        (const void*)masked_stream_kernel<kF32, kModeKey>,
-        (const void*)masked_stream_kernel<kF32, kModeVerify>,
-    };
-    for (const void* f : fns)
-      if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (e != cudaSuccess) {
-      (void)cudaGetLastError();
-      return 0;
-    }
-    sms[dev] = n;
-  }
-  return sms[dev];
-}
-
-// Launches the streaming form when the option allows it and the shape and buffers suit it:
-// bf16 / f16 / f32; 16-byte aligned logits rows whose length is a whole number of 16-byte
-// vectors; 16-byte aligned mask rows of a multiple of 4 words; a workspace for the row (and
-// verify group) slots. `aligned` covers the pointer and stride checks of the caller.
-// Returns false (nothing launched) otherwise.
-template <int MODE>
-static bool dispatch_stream(int dt, bool aligned, ScanParams& p, void* ws, size_t ws_bytes,
-                            int64_t groups, cudaStream_t s, bool pdl, cudaError_t* err) {
-  const int64_t opt = option(ONYX_OPTION_STREAM);
-  if (opt == ONYX_STREAM_NEVER || !aligned) return false;
-  if (dt != kBF16 && dt != kF16 && dt != kF32) return false;
-  if (MODE == kModeVerify && p.per_group > 32) return false;
-  const int es = dtype_bytes(dt);
-  if ((p.vocab * es) % 16 != 0 || ((p.vocab + 31) / 32) % 4 != 0) return false;
-  if (opt == ONYX_STREAM_AUTO && p.rows * p.vocab * es < kStreamAutoMinBytes) return false;
-  const int64_t units = p.rows * ((p.vocab + kStreamUnit - 1) / kStreamUnit);
-  if (units > 0x7FFFFFFFll) return false;
-  const size_t need = stream_workspace_bytes(p.rows, groups, p.vocab, p.per_group);
-  if (need && (!ws || ws_bytes < need || ((uintptr_t)ws & 255u))) return false;
-  const int sms = stream_device_sms();
-  if (sms <= 0) return false;
-  const int ctas = (int)std::min<int64_t>(sms, units);
-  const size_t row_bytes =
-      (p.vocab > kStreamUnit) ? align_up((size_t)p.rows * sizeof(ulonglong2), 256) : 0;
-  p.row_slots = static_cast<ulonglong2*>(ws);
-  p.group_slots = reinterpret_cast<ulonglong2*>(static_cast<char*>(ws) + row_bytes);
-  switch (dt) {
-    case kBF16: *err = launch_stream_t<kBF16, MODE>(p, ctas, s, pdl); break;
-    case kF16: *err = launch_stream_t<kF16, MODE>(p, ctas, s, pdl); break;
-    default: *err = launch_stream_t<kF32, MODE>(p, ctas, s, pdl); break;
-  }
-  return true;
-}
-
-static bool mask_rows_aligned(const uint32_t* m, int64_t stride_a, int64_t stride_b) {
-  return aligned16(m) && stride_a % 4 == 0 && stride_b % 4 == 0;
-}
-
 }  // namespace onyx
 
 using namespace onyx;
@@ -1452,10 +1340,6 @@ int onyx_set_option(int id, int64_t value) {
     case ONYX_OPTION_CLUSTER:
     case ONYX_OPTION_PDL:
       if (value != 0 && value != 1) return ONYX_ERR_INVALID_ARGUMENT;
-      break;
-    case ONYX_OPTION_STREAM:
-      if (value != ONYX_STREAM_NEVER && value != ONYX_STREAM_ALWAYS && value != ONYX_STREAM_AUTO)
-        return ONYX_ERR_INVALID_ARGUMENT;
       break;
     case ONYX_OPTION_SAMPLE_FORM:
       if (value < -1 || value > kCsMaxCluster) return ONYX_ERR_INVALID_ARGUMENT;
@@ -1493,17 +1377,15 @@ size_t onyx_masked_argmax_workspace_size(int64_t rows, int64_t vocab, int dtype)
   if (rows <= 0 || vocab <= 0 || !dtype_ok(dtype)) return 0;
   // worst case over alignments: the generic plan has the most segments
   const Plan a = make_plan(dtype, vocab, true), b = make_plan(dtype, vocab, false);
-  return std::max({workspace_bytes_for(rows, rows, a, 1), workspace_bytes_for(rows, rows, b, 1),
-                   stream_workspace_bytes(rows, rows, vocab, 1)});
+  return std::max(workspace_bytes_for(rows, rows, a, 1), workspace_bytes_for(rows, rows, b, 1));
 }
 
 size_t onyx_spec_verify_workspace_size(int64_t batch, int64_t gamma, int64_t vocab, int dtype) {
   if (batch <= 0 || gamma < 1 || vocab <= 0 || !dtype_ok(dtype)) return 0;
   const int64_t rows = batch * (gamma + 1);
   const Plan a = make_plan(dtype, vocab, true), b = make_plan(dtype, vocab, false);
-  return std::max({workspace_bytes_for(rows, batch, a, (int)(gamma + 1)),
-                   workspace_bytes_for(rows, batch, b, (int)(gamma + 1)),
-                   stream_workspace_bytes(rows, batch, vocab, (int)(gamma + 1))});
+  return std::max(workspace_bytes_for(rows, batch, a, (int)(gamma + 1)),
+                  workspace_bytes_for(rows, batch, b, (int)(gamma + 1)));
 }
 
 static int common_checks(const void* logits, int dtype, int64_t rows, int64_t vocab,
@@ -1543,10 +1425,6 @@ int onyx_masked_argmax(const void* logits, int dtype, int64_t rows, int64_t voca
   p.out_idx = out_idx;
   p.out_status = out_status;
   cudaError_t cluster_err = cudaSuccess;
-  if (mask && dispatch_stream<kModeArgmax>(dtype, aligned && mask_rows_aligned(mask, rows > 1 ? mask_stride : 0, 0),
-                                           p, workspace, workspace_bytes, rows,
-                                           (cudaStream_t)stream, pdl_enabled(), &cluster_err))
-    return finish_launch(cluster_err);
   if (dispatch_cluster<kModeArgmax>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled(),
                                     &cluster_err))
     return finish_launch(cluster_err);  // one cluster per row: no workspace involved
@@ -1585,10 +1463,6 @@ int onyx_gather_masked_argmax(const void* logits, int dtype, int64_t rows, int64
   p.out_idx = out_idx;
   p.out_status = out_status;
   cudaError_t cluster_err = cudaSuccess;
-  if (dispatch_stream<kModeArgmax>(dtype, aligned && mask_rows_aligned(table, table_stride, 0), p,
-                                   workspace, workspace_bytes, rows, (cudaStream_t)stream,
-                                   pdl_enabled(), &cluster_err))
-    return finish_launch(cluster_err);
   if (dispatch_cluster<kModeArgmax>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled(),
                                     &cluster_err))
     return finish_launch(cluster_err);  // one cluster per row: no workspace involved
@@ -1638,14 +1512,6 @@ int onyx_spec_verify(const void* logits, int dtype, int64_t batch, int64_t gamma
   p.bonus = bonus ? 1 : 0;
   p.accept_len = accept_len;
   p.correction = correction;
-  {
-    cudaError_t stream_err = cudaSuccess;
-    const bool masks_ok = mask_rows_aligned(masks, batch > 1 ? mask_batch_stride : 0,
-                                            mask_row_stride);
-    if (dispatch_stream<kModeVerify>(dtype, aligned && masks_ok, p, workspace, workspace_bytes,
-                                     batch, (cudaStream_t)stream, pdl_enabled(), &stream_err))
-      return finish_launch(stream_err);
-  }
   const int rc = bind_workspace(p, workspace, workspace_bytes,
                                 workspace_bytes_for(p.rows, batch, pl, P), batch);
   if (rc) return rc;
@@ -1692,10 +1558,6 @@ int onyx_vocab_partial_argmax(const void* logits, int dtype, int64_t rows, int64
   p.seg_elems = pl.seg_elems;
   p.out_key = reinterpret_cast<unsigned long long*>(out_keys);
   cudaError_t cluster_err = cudaSuccess;
-  if (dispatch_stream<kModeKey>(dtype, aligned && mask_rows_aligned(mask, rows > 1 ? mask_stride : 0, 0),
-                                p, workspace, workspace_bytes, rows, (cudaStream_t)stream,
-                                pdl_enabled(), &cluster_err))
-    return finish_launch(cluster_err);
   if (dispatch_cluster<kModeKey>(dtype, pl.fast, p, (cudaStream_t)stream, pdl_enabled(),
                                     &cluster_err))
     return finish_launch(cluster_err);  // one cluster per row: no workspace involved
@@ -2114,10 +1976,7 @@ int onyx_vocab_exchange_argmax(const void* logits, int dtype, int64_t rows, int6
   x.out_status = out_status;
   const bool pdl = pdl_enabled();
   cudaError_t err = cudaSuccess;
-  if (!dispatch_stream<kModeKey>(dtype, aligned && mask_rows_aligned(mask, rows > 1 ? mask_stride : 0, 0),
-                                 p, workspace, workspace_bytes, rows, (cudaStream_t)stream, pdl,
-                                 &err) &&
-      !dispatch_cluster<kModeKey>(dtype, pl.fast, p, (cudaStream_t)stream, pdl, &err)) {
+  if (!dispatch_cluster<kModeKey>(dtype, pl.fast, p, (cudaStream_t)stream, pdl, &err)) {
     rc = bind_workspace(p, workspace, workspace_bytes, workspace_bytes_for(rows, rows, pl, 1), rows);
     if (rc) return rc;
     err = dispatch<kModeKey>(dtype, pl.fast, p, (cudaStream_t)stream, pdl);

@@ -38,11 +38,8 @@ def test_abi_version_and_error_strings(cuda_lib):
 
 
 def test_workspace_sizes(cuda_lib):
-    # rows of one 256-element unit are never split: no workspace
-    assert cuda_lib.onyx_masked_argmax_workspace_size(4, 256, _lib.DTYPE_BF16) == 0
-    # longer rows may be split over CTAs by the streaming form: one 16-byte slot per row
-    assert cuda_lib.onyx_masked_argmax_workspace_size(4, 1000, _lib.DTYPE_BF16) == 256
-    assert cuda_lib.onyx_masked_argmax_workspace_size(20, 1000, _lib.DTYPE_BF16) == 512
+    # a single segment needs no workspace
+    assert cuda_lib.onyx_masked_argmax_workspace_size(4, 1000, _lib.DTYPE_BF16) == 0
     # 64 rows of 128,256 bf16 split into segments: partials + counters, 256-aligned
     n = cuda_lib.onyx_masked_argmax_workspace_size(64, 128256, _lib.DTYPE_BF16)
     assert n > 0 and n % 256 == 0
@@ -71,22 +68,20 @@ def test_argument_errors_are_reported_before_any_launch(cuda_lib):
 
 
 def test_options_round_trip_and_reject_bad_values(cuda_lib):
-    saved = {k: _lib.get_option(k) for k in range(5)}
+    saved = {k: _lib.get_option(k) for k in range(4)}
     try:
-        assert saved[_lib.OPTION_STREAM] in (_lib.STREAM_NEVER, _lib.STREAM_ALWAYS,
-                                             _lib.STREAM_AUTO)
-        for k, v in ((_lib.OPTION_STREAM, _lib.STREAM_ALWAYS), (_lib.OPTION_CLUSTER, 0),
-                     (_lib.OPTION_PDL, 0), (_lib.OPTION_SAMPLE_FORM, -1),
+        assert saved[_lib.OPTION_CLUSTER] in (0, 1) and saved[_lib.OPTION_PDL] in (0, 1)
+        for k, v in ((_lib.OPTION_CLUSTER, 0), (_lib.OPTION_PDL, 0), (_lib.OPTION_SAMPLE_FORM, -1),
                      (_lib.OPTION_TEST_WITHHELD_KEY_BYTES, 8)):
             _lib.set_option(k, v)
             assert _lib.get_option(k) == v
-        for k, v in ((_lib.OPTION_STREAM, 3), (_lib.OPTION_CLUSTER, 2), (_lib.OPTION_SAMPLE_FORM, 17),
-                     (_lib.OPTION_TEST_WITHHELD_KEY_BYTES, -1), (5, 0), (-1, 0)):
+        for k, v in ((_lib.OPTION_CLUSTER, 2), (_lib.OPTION_PDL, -1), (_lib.OPTION_SAMPLE_FORM, 17),
+                     (_lib.OPTION_TEST_WITHHELD_KEY_BYTES, -1), (4, 0), (-1, 0)):
             assert cuda_lib.onyx_set_option(k, v) == _lib.ERR_INVALID_ARGUMENT
-        assert cuda_lib.onyx_get_option(5) == -1
-        with _lib.option_override({_lib.OPTION_STREAM: _lib.STREAM_NEVER}):
-            assert _lib.get_option(_lib.OPTION_STREAM) == _lib.STREAM_NEVER
-        assert _lib.get_option(_lib.OPTION_STREAM) == _lib.STREAM_ALWAYS
+        assert cuda_lib.onyx_get_option(4) == -1
+        with _lib.option_override({_lib.OPTION_CLUSTER: 1}):
+            assert _lib.get_option(_lib.OPTION_CLUSTER) == 1
+        assert _lib.get_option(_lib.OPTION_CLUSTER) == 0
     finally:
         for k, v in saved.items():
             _lib.set_option(k, v)

@@ -220,20 +220,12 @@ def test_workspace_is_left_zeroed_across_layouts(cuda_lib):
             assert int(torch.count_nonzero(buf)) == 0
 
 
-PATHS = {
-    "cluster": {_lib.OPTION_STREAM: _lib.STREAM_NEVER, _lib.OPTION_CLUSTER: 1},
-    "ticket": {_lib.OPTION_STREAM: _lib.STREAM_NEVER, _lib.OPTION_CLUSTER: 0},
-    "stream": {_lib.OPTION_STREAM: _lib.STREAM_ALWAYS, _lib.OPTION_CLUSTER: 1},
-}
-
-
-@pytest.mark.parametrize("path", list(PATHS))
-def test_every_cross_cta_combine_matches_oracle(path, cuda_lib):
+@pytest.mark.parametrize("path", ["cluster", "ticket"])
+def test_both_cross_cta_combines_match_oracle(path, cuda_lib):
     """Rows that fit one thread-block cluster merge CTA partials through distributed shared
-    memory; the CLUSTER option off forces the global-ticket merge; the STREAM option on
-    forces the streaming form (split rows merged by 128-bit compare-and-swap). All must
-    agree with the oracle for argmax, gather and shard keys."""
-    with _lib.option_override(PATHS[path]):
+    memory; the CLUSTER option off forces the global-ticket merge. Both must agree with the
+    oracle for argmax, gather and shard keys."""
+    with _lib.option_override({_lib.OPTION_CLUSTER: 1 if path == "cluster" else 0}):
         _combine_cases()
 
 

@@ -31,8 +31,7 @@ def _inputs(rows, vocab=128256, seed=4):
 def test_withheld_keys_time_out_and_the_context_recovers(cuda_lib):
     x, m = _inputs(2)
     xd, md = to_device(x, "bf16"), masks_to_device(m)
-    with _lib.option_override({_lib.OPTION_STREAM: _lib.STREAM_NEVER, _lib.OPTION_CLUSTER: 1,
-                               _lib.OPTION_TEST_WITHHELD_KEY_BYTES: 8}):
+    with _lib.option_override({_lib.OPTION_CLUSTER: 1, _lib.OPTION_TEST_WITHHELD_KEY_BYTES: 8}):
         _withheld_calls(xd, md)
 
     idx_ref, st_ref = oracle.masked_argmax(x, m, dtype="bf16")
