@@ -843,9 +843,9 @@ __device__ __forceinline__ void cluster_select(const ScanParams& p) {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncwarp();
-  // First phase of the cluster barrier: its completion, awaited just before the first
-  // access to another CTA's shared memory, guarantees every CTA of the cluster is running
-  // and rank 0's mbarrier is initialised.
+  // First phase of the cluster barrier: its completion guarantees every CTA of the cluster
+  // is running and rank 0's mbarrier is initialised, before any access to another CTA's
+  // shared memory (step 4). It is awaited while the segment's loads are in flight.
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
@@ -860,8 +860,9 @@ __device__ __forceinline__ void cluster_select(const ScanParams& p) {
   if (active) {
     const int64_t e0 = (int64_t)seg_id * p.seg_elems;
     seg.load(row_base, mrow, e0, min(e0 + p.seg_elems, p.vocab), lane);
-    wmax = (uint32_t)seg.max_code();
   }
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+  if (active) wmax = (uint32_t)seg.max_code();
   asm volatile("griddepcontrol.launch_dependents;" :::);
 
   // 2. CTA maximum, known to every warp after one CTA barrier
@@ -878,7 +879,6 @@ __device__ __forceinline__ void cluster_select(const ScanParams& p) {
   // 4. each CTA's key (maximum << 32 | ~lowest index) into rank 0's shared memory: rank 0
   //    stores its own; every other CTA stores asynchronously, the store's completion counted
   //    on rank 0's mbarrier, which completes once every key has landed
-  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
   if (warp == 0) {
     const uint32_t cidx = __reduce_min_sync(kFull, lane < nwarps ? s_widx[lane] : 0xFFFFFFFFu);
     if (lane == 0) {
