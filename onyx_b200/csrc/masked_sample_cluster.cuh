@@ -216,6 +216,60 @@ __device__ __forceinline__ int cs_nth_bit8(uint32_t m, uint32_t r) {
   return 7;
 }
 
+// ---- per-value table (bf16) -------------------------------------------------------------
+// A bf16 weight exp((v - max) / T) depends only on the 16-bit value, and a row's values
+// cluster in a few binary exponents. The table has one bin per value whose exponent field lies
+// in the kVtExps exponents below and at the row's largest finite one, for each sign, in
+// descending value order: bins [0, kVtHalf) the positive values from the largest down,
+// [kVtHalf, kVtBins) the negative ones from the smallest magnitude down. Zeros and magnitudes
+// below the table form the "small" region, which lies between the two halves in value order;
+// its ids keep a per-id weight.
+constexpr int kVtExps = 16;
+constexpr int kVtHalf = kVtExps * 128;
+constexpr int kVtBins = 2 * kVtHalf;
+static_assert(kVtBins * (sizeof(double) + sizeof(uint32_t)) <= sizeof(WarpBuf) * kCsWarps,
+              "the per-value table overlays the compaction buffers");
+
+// largest exponent field among the valid (bit set in `bits`), finite bf16 values of a vector
+// of eight; 0 if none
+__device__ __forceinline__ uint32_t vt_max_exponent(const uint4& a, uint32_t bits) {
+  uint32_t m01, m23, m45, m67;
+  expand8_16(bits, m01, m23, m45, m67);
+  const uint32_t w[4] = {a.x & m01, a.y & m23, a.z & m45, a.w & m67};
+  uint32_t best = 0u;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t e = (w[i] >> 7) & 0x00FF00FFu;  // both halves' exponent fields
+    e &= ~__vcmpeq2(e, 0x00FF00FFu);          // infinities and NaN are not finite
+    best = __vmaxu2(best, e);
+  }
+  return max(best & 0xFFFFu, best >> 16);
+}
+
+// table bin of a finite bf16 bit pattern h, or -1 for the small region
+__device__ __forceinline__ int vt_bin(uint32_t h, int e_top) {
+  if ((h & 0x7FFFu) == 0u) return -1;  // +-0
+  const int de = e_top - (int)((h >> 7) & 0xFFu);
+  if (de < 0 || de >= kVtExps) return -1;  // (de < 0: an infinity, never weighted here)
+  const int m = (int)(h & 0x7Fu);
+  return (h & 0x8000u) ? kVtHalf + (kVtExps - 1 - de) * 128 + m : de * 128 + (127 - m);
+}
+
+// the bf16 value of table bin b (a NaN for a bin below exponent 0, which holds no value)
+__device__ __forceinline__ float vt_value(int b, int e_top) {
+  const bool neg = b >= kVtHalf;
+  const int r = neg ? b - kVtHalf : b;
+  const int de = neg ? kVtExps - 1 - (r >> 7) : (r >> 7);
+  const int m = neg ? (r & 127) : 127 - (r & 127);
+  const int e = e_top - de;
+  if (e < 0) return __int_as_float(0x7FC00000);
+  return bf16_bits_to_f32((neg ? 0x8000u : 0u) | ((uint32_t)e << 7) | (uint32_t)m);
+}
+
+// bins of the combined area per row (split over the cluster): the radix levels' widest level,
+// or for bf16 the per-value table
+__host__ __device__ constexpr int cs_comb_bins(int dt) { return dt == kBF16 ? kVtBins : kCsBins; }
+
 template <int DT>
 __global__ void __launch_bounds__(kCsThreads, 1)
     masked_sample_cluster_kernel(const ClusterSampleParams p) {
@@ -229,6 +283,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   __shared__ uint32_t s_u[kSampleWarps];
   __shared__ double s_wmass[kCsWarps];    // per warp: total weight, then kept mass above the cut
   __shared__ uint32_t s_wcount[kCsWarps];  // per warp: +inf ids, then ties of the cut value
+  __shared__ uint32_t s_wexp[kCsWarps];    // per warp: largest finite exponent field (bf16)
   __shared__ uint32_t s_bin, s_ties;
   __shared__ double s_above;
   __shared__ long long s_take;
@@ -248,7 +303,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   uint32_t* const s_words = p.mask ? reinterpret_cast<uint32_t*>(s_dyn + p.off_words) : nullptr;
   WarpBuf* const s_bufs = reinterpret_cast<WarpBuf*>(s_dyn + p.off_work);
   CsHist* const s_hist = reinterpret_cast<CsHist*>(s_dyn + p.off_work);
-  const int comb_cap = (kCsBins + k - 1) / k;
+  const int comb_cap = (cs_comb_bins(DT) + k - 1) / k;
   double* const s_comb_p = reinterpret_cast<double*>(s_dyn + p.off_comb);
   uint32_t* const s_comb_c =
       reinterpret_cast<uint32_t*>(s_dyn + p.off_comb + ((comb_cap * 8 + 15) & ~15));
@@ -288,7 +343,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
 
   // 1. support: the masked, NaN-propagating maximum (packed pairs for 16-bit types); any
   //    valid id at all
-  uint32_t any = 0u, lcode;
+  uint32_t any = 0u, lcode, lexp = 0u;
   {
     float lmax = -INFINITY;
     uint32_t pm = 0u;
@@ -308,6 +363,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       } else {
         const uint4 a = *reinterpret_cast<const uint4*>(s_vals + (size_t)j0 * 2);
         pm = Packed16<DT>::pmax(pm, Packed16<DT>::masked_pair_max(a, m));
+        if constexpr (DT == kBF16) lexp = max(lexp, vt_max_exponent(a, m));
       }
     }
     if constexpr (DT != kF32) lmax = Packed16<DT>::pair_to_f32_max(pm);
@@ -315,20 +371,24 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   }
   {
     const uint32_t wa = __reduce_or_sync(kFull, any), wc = __reduce_max_sync(kFull, lcode);
+    const uint32_t we = __reduce_max_sync(kFull, lexp);
     if (lane == 0) {
       s_wcount[warp] = wa;
       s_u[warp] = wc;
+      s_wexp[warp] = we;
     }
     __syncthreads();
     CsMail m = {};
     m.u[0] = __reduce_or_sync(kFull, s_wcount[lane]);
     m.u[1] = __reduce_max_sync(kFull, s_u[lane]);
+    m.u[2] = __reduce_max_sync(kFull, s_wexp[lane]);
     exchange(m);  // (its barriers also end every read of s_wcount and s_u)
   }
-  uint32_t c_any = 0u, c_code = 0u;
+  uint32_t c_any = 0u, c_code = 0u, c_exp = 0u;
   for (int q = 0; q < k; ++q) {
     c_any |= s_all[q].u[0];
     c_code = max(c_code, s_all[q].u[1]);
+    c_exp = max(c_exp, s_all[q].u[2]);
   }
   constexpr uint32_t kOrd32PosInf = 0xFF800000u;
   const uint32_t status = !c_any ? kStatusEmptyMask
@@ -441,52 +501,210 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     // divide by T, as the reference does: multiplying by 1/T rounds differently
     auto weight_exact = [&](float x) { return exp(((double)x - vmax) / p.temperature); };
 
-    // 3. total weight and the number of weighted ids
-    double tsum = 0.0;
-    uint32_t nw = 0u;
-    cs_warp_batches<DT>(
-        s_vals, s_words, wlo, whi, &s_bufs[warp],
-        [&](int, const float* v, uint32_t m) {
-          uint32_t keep = 0u;
-#pragma unroll
-          for (int t = 0; t < 8; ++t)
-            if (((m >> t) & 1u) && v[t] != -INFINITY) keep |= 1u << t;
-          return keep;
-        },
-        [&](bool has, int, float x) {
-          if (has) {
-            const double w = weight_exact(x);
-            if (w > 0.0) {
-              tsum += w;
-              ++nw;
-            }
-          }
-          return false;
-        });
-    {
-      const double wt = warp_sum_d(tsum);
-      const uint32_t wn = __reduce_add_sync(kFull, nw);
-      if (lane == 0) {
-        s_wmass[warp] = wt;
-        s_wcount[warp] = wn;
-      }
-    }
-    __syncthreads();
-    {
-      double ct = 0.0;
-      for (int w2 = 0; w2 < kCsWarps; ++w2) ct += s_wmass[w2];
-      CsMail m = {};
-      m.d[0] = ct;
-      m.u[0] = __reduce_add_sync(kFull, s_wcount[lane]);
-      exchange(m);
-    }
+    const bool keep_all = !(p.top_p < 1.0);
     double total = 0.0;
     uint32_t nwt = 0u;
-    for (int q = 0; q < k; ++q) {
-      total += s_all[q].d[0];
-      nwt += s_all[q].u[0];
+    uint32_t vstar = 0u;  // order code of the cut value (0: below every value: keep all)
+    uint32_t ties = 0u;
+    double above = 0.0;  // probability of every id ranked above the current prefix
+    bool have_cut = keep_all;  // the cut is known (nothing to cut with top_p = 1)
+    // bf16: the per-value table; steps 5 and 6 then look probabilities up instead of
+    // computing exp per id (while use_table holds)
+    bool use_table = false;
+    const int e_top = (int)c_exp;
+    double* const s_tp = reinterpret_cast<double*>(s_dyn + p.off_work);  // [kVtBins] p per id
+    uint32_t* const s_tc = reinterpret_cast<uint32_t*>(s_dyn + p.off_work + kVtBins * 8);
+    if constexpr (DT == kBF16) {
+      use_table = true;
+      // 3t. this CTA's counts per bin (into the count half of the work area) and the per-id
+      //     weights of its small-region ids
+      for (int b = tid; b < kVtBins; b += kCsThreads) s_tc[b] = 0u;
+      __syncthreads();
+      double fsum = 0.0;
+      uint32_t fn = 0u;
+      for (int s = wlo; s < whi; s += kSampleStep) {
+        float v[8];
+        const uint32_t m = cs_load8<DT>(s_vals, s_words, s + 8 * lane, whi, v);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          if (!((m >> t) & 1u) || v[t] == -INFINITY) continue;
+          const int b = vt_bin(__float_as_uint(v[t]) >> 16, e_top);
+          if (b >= 0) {
+            atomicAdd(&s_tc[b], 1u);
+          } else {
+            const double w = weight_exact(v[t]);
+            if (w > 0.0) {
+              fsum += w;
+              ++fn;
+            }
+          }
+        }
+      }
+      cs_cluster_sync();  // every CTA's counts are complete
+      // 3u. this CTA's share of the bins: counts summed over the cluster in rank order, one
+      //     exp per nonempty bin; zero weights drop out
+      const int per = (kVtBins + k - 1) / k;
+      const int b0 = (int)rank * per, b1 = min(kVtBins, b0 + per);
+      double smass = 0.0;
+      uint32_t sn = 0u;
+      for (int b = b0 + tid; b < b1; b += kCsThreads) {
+        uint32_t cq[kCsMaxCluster];
+#pragma unroll
+        for (int q = 0; q < kCsMaxCluster; ++q) cq[q] = q < k ? cs_remote(s_tc, (uint32_t)q)[b] : 0u;
+        uint32_t csum = 0u;
+#pragma unroll
+        for (int q = 0; q < kCsMaxCluster; ++q) csum += cq[q];
+        double w = 0.0;
+        if (csum) {
+          w = weight_exact(vt_value(b, e_top));
+          if (!(w > 0.0)) {
+            w = 0.0;
+            csum = 0u;
+          }
+        }
+        s_comb_p[b - b0] = w;
+        s_comb_c[b - b0] = csum;
+        smass += (double)csum * w;
+        sn += csum;
+      }
+      {
+        const double wm = warp_sum_d(smass + fsum), wf = warp_sum_d(fsum);
+        const uint32_t wn = __reduce_add_sync(kFull, sn + fn);
+        if (lane == 0) {
+          s_wmass[warp] = wm;
+          s_red[warp] = wf;
+          s_wcount[warp] = wn;
+        }
+      }
+      __syncthreads();
+      {
+        double cm = 0.0, cf = 0.0;
+        for (int w2 = 0; w2 < kCsWarps; ++w2) {
+          cm += s_wmass[w2];
+          cf += s_red[w2];
+        }
+        CsMail m = {};
+        m.d[0] = cm;
+        m.d[1] = cf;
+        m.u[0] = __reduce_add_sync(kFull, s_wcount[lane]);
+        exchange(m);  // (its cluster barrier also completes every CTA's share)
+      }
+      double small_w = 0.0;
+      for (int q = 0; q < k; ++q) {
+        total += s_all[q].d[0];
+        small_w += s_all[q].d[1];
+        nwt += s_all[q].u[0];
+      }
+      // 3v. the whole table in this CTA: probability and count per bin (every remote read of
+      //     the local counts ended at the exchange)
+      for (int b = tid; b < kVtBins; b += kCsThreads) {
+        const int q = b / per, o = b - q * per;
+        const double w = cs_remote(s_comb_p, (uint32_t)q)[o];
+        s_tc[b] = cs_remote(s_comb_c, (uint32_t)q)[o];
+        s_tp[b] = w / total;
+      }
+      __syncthreads();
+      // 3w. the cut: ranked by value, the bin where the cumulative probability reaches top_p.
+      //     Thread t owns bins 4t .. 4t+3; the small region follows bin kVtHalf - 1. Every
+      //     CTA scans the same table and finds the same cut.
+      if (!keep_all) {
+        static_assert(kVtBins == 4 * kCsThreads, "four bins per thread");
+        const double small_p = small_w / total;
+        double pb[4];
+        uint32_t cb[4];
+        double tm = 0.0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          cb[i] = s_tc[4 * tid + i];
+          pb[i] = (double)cb[i] * s_tp[4 * tid + i];
+          tm += pb[i];
+        }
+        const bool small_after = 4 * tid + 3 == kVtHalf - 1;
+        if (small_after) tm += small_p;
+        double sum_all;
+        const double before = block_exclusive_scan_d(tm, s_red, &sum_all);
+        if (tid == 0) s_bin = 0xFFFFFFFFu;
+        __syncthreads();
+        // the earliest crossing in value order (rank 2b for bin b, 2 kVtHalf - 1 for the small
+        // region); a block-scan rounding could let two threads see one
+        double cum = before;
+        uint32_t mine = 0xFFFFFFFFu;
+        double mine_before = 0.0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (cb[i] && cum < p.top_p && cum + pb[i] >= p.top_p && mine == 0xFFFFFFFFu) {
+            mine = 2u * (uint32_t)(4 * tid + i);
+            mine_before = cum;
+          }
+          cum += pb[i];
+        }
+        if (small_after && mine == 0xFFFFFFFFu && small_p > 0.0 && cum < p.top_p &&
+            cum + small_p >= p.top_p)
+          mine = 2u * kVtHalf - 1u;
+        if (mine != 0xFFFFFFFFu) atomicMin(&s_bin, mine);
+        __syncthreads();
+        if (mine != 0xFFFFFFFFu && mine == s_bin && !(mine & 1u)) {
+          s_above = mine_before;
+          s_ties = cb[(mine >> 1) - 4 * tid];
+        }
+        __syncthreads();
+        const uint32_t cut = s_bin;
+        if (cut != 0xFFFFFFFFu && !(cut & 1u)) {
+          have_cut = true;
+          vstar = ord32(vt_value((int)(cut >> 1), e_top));
+          above = s_above;
+          ties = s_ties;
+        }
+        __syncthreads();  // every thread has read s_bin, s_above, s_ties
+      }
+      // without a cut here (it falls among the small-region ids, or the sum never reaches
+      // top_p), the radix levels below find it; they overwrite the table
+      if (!have_cut) use_table = false;
+    } else {
+      // 3. total weight and the number of weighted ids
+      double tsum = 0.0;
+      uint32_t nw = 0u;
+      cs_warp_batches<DT>(
+          s_vals, s_words, wlo, whi, &s_bufs[warp],
+          [&](int, const float* v, uint32_t m) {
+            uint32_t keep = 0u;
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              if (((m >> t) & 1u) && v[t] != -INFINITY) keep |= 1u << t;
+            return keep;
+          },
+          [&](bool has, int, float x) {
+            if (has) {
+              const double w = weight_exact(x);
+              if (w > 0.0) {
+                tsum += w;
+                ++nw;
+              }
+            }
+            return false;
+          });
+      {
+        const double wt = warp_sum_d(tsum);
+        const uint32_t wn = __reduce_add_sync(kFull, nw);
+        if (lane == 0) {
+          s_wmass[warp] = wt;
+          s_wcount[warp] = wn;
+        }
+      }
+      __syncthreads();
+      {
+        double ct = 0.0;
+        for (int w2 = 0; w2 < kCsWarps; ++w2) ct += s_wmass[w2];
+        CsMail m = {};
+        m.d[0] = ct;
+        m.u[0] = __reduce_add_sync(kFull, s_wcount[lane]);
+        exchange(m);
+      }
+      for (int q = 0; q < k; ++q) {
+        total += s_all[q].d[0];
+        nwt += s_all[q].u[0];
+      }
     }
-    const bool keep_all = !(p.top_p < 1.0);
     // candidates: weight >= tau = (1 - top_p) total / (2 n), i.e. value >= vtau; as a float
     // test, x >= fthr with fthr the least float not below vtau
     const double tau = (1.0 - p.top_p) * total / (2.0 * (double)nwt);
@@ -495,10 +713,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     if ((double)fthr < vtau) fthr = nextafterf(fthr, INFINITY);
 
     // 4. radix levels from below the candidates' common prefix down to one exact value
-    uint32_t vstar = 0u;  // order code of the cut value (0: below every value: keep all)
-    uint32_t ties = 0u;
-    double above = 0.0;  // probability of every id ranked above the current prefix
-    if (!keep_all) {
+    if (!have_cut) {
       const uint32_t lowc = fthr == -INFINITY ? kOrd32NegInf + 1u : min(ord32(fthr), c_maxo);
       const uint32_t diff = lowc ^ c_maxo;
       int top = diff ? 32 - __clz(diff) : 0;  // bits [top, 32) are the same in every candidate
@@ -652,10 +867,39 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     __syncthreads();  // (also: every warp is done with the histogram before the buffers)
     const uint32_t take = (uint32_t)s_take;
 
+    // probability of one kept id: the table's entry for its value, or exp per id
+    auto prob = [&](float x) -> double {
+      if (use_table) {
+        const int b = vt_bin(__float_as_uint(x) >> 16, e_top);
+        if (b >= 0) return s_tp[b];
+      }
+      return weight_exact(x) / total;
+    };
+
     // 5. per warp: probability of the ids ranked above the cut value, and the ties
     double wabove = 0.0;
     uint32_t wties = 0u;
-    if (keep_all) {
+    if (DT == kBF16) {
+      // (the per-value path keeps no per-warp totals and no compaction buffers: one pass of
+      // lookups, ids of the small region weighted one by one)
+      double acc = 0.0;
+      uint32_t lane_ties = 0u;
+      for (int s = wlo; s < whi; s += kSampleStep) {
+        float v[8];
+        const uint32_t m = cs_load8<DT>(s_vals, s_words, s + 8 * lane, whi, v);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          if (!((m >> t) & 1u)) continue;
+          if (v[t] > vstar_f) {
+            acc += prob(v[t]);
+          } else if (!keep_all && v[t] == vstar_f) {
+            ++lane_ties;
+          }
+        }
+      }
+      wabove = warp_sum_d(acc);
+      wties = __reduce_add_sync(kFull, lane_ties);
+    } else if (keep_all) {
       wabove = s_wmass[warp] / total;
     } else {
       uint32_t lane_ties = 0u;
@@ -762,7 +1006,82 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       }
     }
     __syncthreads();
-    if (warp == s_walk_warp) {
+    if (warp == s_walk_warp && DT == kBF16) {
+      // 6. the draw: walk this warp's kept ids in id order with running sums; one step of
+      //    256 ids at a time, each lane's eight in id order after the lanes before it
+      double cum = s_walk_before;
+      uint32_t tie_rank = (uint32_t)s_walk_rank;  // ties of the cut value before this step
+      int pick = -1, last = -1;  // slice-relative
+      for (int s = wlo; s < whi && pick < 0; s += kSampleStep) {  // warp-uniform
+        const int j0 = s + 8 * lane;
+        float v[8];
+        const uint32_t m = cs_load8<DT>(s_vals, s_words, j0, whi, v);
+        uint32_t above_bits = 0u, tie_bits = 0u;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          if (!((m >> t) & 1u)) continue;
+          if (v[t] > vstar_f) above_bits |= 1u << t;
+          if (!keep_all && v[t] == vstar_f) tie_bits |= 1u << t;
+        }
+        const uint32_t c = __popc(tie_bits);
+        uint32_t incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t t = __shfl_up_sync(kFull, incl, o);
+          if (lane >= o) incl += t;
+        }
+        uint32_t r = tie_rank + incl - c;
+        tie_rank += __shfl_sync(kFull, incl, 31);
+        uint32_t keep = above_bits;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          if ((tie_bits >> t) & 1u) {
+            if (r < take) keep |= 1u << t;
+            ++r;
+          }
+        }
+        double pl[8];
+        double lsum = 0.0;
+        int llast = -1;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          pl[t] = ((keep >> t) & 1u) ? prob(v[t]) : 0.0;
+          lsum += pl[t];
+          if (pl[t] > 0.0) llast = j0 + t;
+        }
+        double run = lsum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const double t = __shfl_up_sync(kFull, run, o);
+          if (lane >= o) run += t;
+        }
+        const int sl = (int)__reduce_max_sync(kFull, (uint32_t)(llast + 1)) - 1;
+        if (sl >= 0) last = sl;
+        const unsigned hit = __ballot_sync(kFull, lsum > 0.0 && threshold < cum + run);
+        if (hit) {
+          const int wl = __ffs(hit) - 1;
+          int pk = -1;
+          if (lane == wl) {
+            double r2 = cum + (run - lsum);
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+              if (pl[t] > 0.0 && pk < 0) {
+                r2 += pl[t];
+                if (threshold < r2) pk = j0 + t;
+              }
+            }
+            if (pk < 0) pk = llast;  // the running sums round differently from the scan
+          }
+          pick = __shfl_sync(kFull, pk, wl);
+        }
+        cum += __shfl_sync(kFull, run, 31);
+      }
+      if (pick < 0) pick = last;  // the draw lies past this warp's sum (rounding)
+      if (lane == 0) {
+        p.out_idx[row] = (int32_t)(lo + pick);
+        p.out_status[row] = 0u;
+      }
+    } else if (warp == s_walk_warp) {
       // 6. the draw: walk this warp's kept ids in id order with running sums
       double cum = s_walk_before;
       uint32_t tie_rank = (uint32_t)s_walk_rank;  // ties of the cut value before this step

@@ -1589,7 +1589,8 @@ struct ClusterSamplePlan {
 static size_t cs_align16(size_t x) { return (x + 15) & ~(size_t)15; }
 
 // shared memory of the cluster form with k CTAs per row (0: it cannot fit)
-static ClusterSamplePlan cs_layout(int k, int64_t vocab, int elem, bool masked) {
+static ClusterSamplePlan cs_layout(int k, int64_t vocab, int dtype, bool masked) {
+  const int elem = dtype == kF32 ? 4 : 2;
   ClusterSamplePlan pl;
   const int64_t per = (vocab + k - 1) / k;
   const int64_t slice = (per + kCsSliceAlign - 1) / kCsSliceAlign * kCsSliceAlign;
@@ -1602,7 +1603,7 @@ static ClusterSamplePlan cs_layout(int k, int64_t vocab, int elem, bool masked) 
   pl.off_work = (int)off;
   off += sizeof(WarpBuf) * kCsWarps;
   pl.off_comb = (int)off;
-  const size_t cap = (kCsBins + k - 1) / k;
+  const size_t cap = (cs_comb_bins(dtype) + k - 1) / k;
   off += cs_align16(cap * 8) + cs_align16(cap * 4);
   pl.smem = off;
   return pl;
@@ -1649,11 +1650,10 @@ static int launch_cluster_sample(int dtype, const SampleParams& sp, int dev, cud
       for (int& x : r) x = -1;
     d.ready = true;
   }
-  const int elem = dtype == kF32 ? 4 : 2;
   const bool masked = sp.mask != nullptr;
   int k_fit = 0;
   for (int k = 1; k <= kCsMaxCluster; ++k) {
-    const ClusterSamplePlan pl = cs_layout(k, sp.vocab, elem, masked);
+    const ClusterSamplePlan pl = cs_layout(k, sp.vocab, dtype, masked);
     if (pl.k && pl.smem <= (size_t)d.max_dyn) {
       k_fit = k;
       break;
@@ -1702,7 +1702,7 @@ static int launch_cluster_sample(int dtype, const SampleParams& sp, int dev, cud
     if (active(cand[i]) >= 1) k = cand[i];
   if (!k) return kNoClusterPlan;
   {
-    const ClusterSamplePlan pl = cs_layout(k, sp.vocab, elem, masked);
+    const ClusterSamplePlan pl = cs_layout(k, sp.vocab, dtype, masked);
     ClusterSampleParams cp = {};
     cp.logits = sp.logits;
     cp.row_stride = sp.row_stride;
