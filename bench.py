@@ -521,10 +521,13 @@ def run_ours(args) -> None:
 
     # ---- timed region -------------------------------------------------------------------
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # NVML starts before the barrier: its start-up takes long enough on a busy box to skew
+    # the ranks' timed regions by more than the peer exchange's wait limit
+    clocks = ClockSampler(local)
     if distributed:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    with ClockSampler(local) as clocks:
+    with clocks:
         gpu_delay(stream)
         start.record(stream)
         if use_graphs:
@@ -542,9 +545,11 @@ def run_ours(args) -> None:
         dist.barrier()
     ms_total = start.elapsed_time(end)
     t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
+    per_rank = [t.clone() for _ in range(world)] if distributed else [t]
     if distributed:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_total = float(t.item())
+        dist.all_gather(per_rank, t)
+    per_rank_ms = [float(x.item()) for x in per_rank]
+    ms_total = max(per_rank_ms)
     ms_per_step = ms_total / args.steps
     total_rows = rows_per_step * args.steps * (world if name != "vocab_parallel" else 1)
     value = total_rows / (ms_total / 1e3)
@@ -635,6 +640,13 @@ def run_ours(args) -> None:
         dist.all_reduce(et, op=dist.ReduceOp.MAX)
     e2e_rows = rows_per_step * e2e_steps * (world if name != "vocab_parallel" else 1)
     e2e_value = e2e_rows / (float(et.item()) / 1e3)
+    # a timed-out exchange wait is sticky: the last step's statuses show whether any wait of
+    # the timed or end-to-end steps gave up (those numbers would not be selections)
+    if name != "spec_verify":
+        last = out_host[(e2e_steps - 1) & 1][1]
+        if bool(((last & ms.STATUS_WAIT_TIMEOUT) != 0).any()):
+            raise RuntimeError(f"rank {rank}: a selection reported a wait timeout; no "
+                               "measurement is printed")
 
     # ---- CPU baseline (rank 0, N=1 only) -----------------------------------------------
     cpu = None
@@ -667,6 +679,7 @@ def run_ours(args) -> None:
         "l2_rotation": f"{R} input sets ({R * set_bytes / 1e6:.0f} MB > 2 x L2 {l2 / 1e6:.0f} MB)",
         "timing": "CUDA events on the launching stream around K graph-replayed steps enqueued "
                   "behind a GPU-side delay, max over ranks",
+        "per_rank_ms_per_step": [round(x / args.steps, 6) for x in per_rank_ms],
         "gbs": achieved,
         "roofline": roofline,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
@@ -714,11 +727,12 @@ def run_dfa_masks(args) -> None:
             builder.masks(states)
     graph.replay()
     stream.synchronize()
+    clocks = ClockSampler(local)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with clocks:
         gpu_delay(stream)
         start.record(stream)
         done = 0
@@ -836,11 +850,12 @@ def run_grammar_row(args) -> None:
     with torch.cuda.stream(stream):
         graph.replay()
     stream.synchronize()
+    clocks = ClockSampler(local)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with clocks:
         gpu_delay(stream)
         start.record(stream)
         done = 0

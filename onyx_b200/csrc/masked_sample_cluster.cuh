@@ -35,6 +35,7 @@ constexpr int kCsWarps = kCsThreads / 32;
 constexpr int kCsMaxCluster = 16;
 constexpr int kCsBins = 2048;   // widest radix level (11 bits)
 constexpr int kCsSliceAlign = 256;  // ids per slice are a multiple of this (8 per lane x 32)
+constexpr int kCsStageGroups = 4;   // copy groups per warp when staging an aligned row
 
 struct ClusterSampleParams {
   const void* logits;
@@ -103,6 +104,21 @@ __device__ __forceinline__ void cs_cp_async4(void* dst, const void* src) {
 
 __device__ __forceinline__ void cs_cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+__device__ __forceinline__ void cs_cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// waits until at most n (0..4) of this thread's committed copy groups are still pending
+__device__ __forceinline__ void cs_cp_async_wait_pending(int n) {
+  switch (n) {
+    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+    case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+    default: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+  }
 }
 
 // Eight staged ids of one lane, from slice-relative id j0 (a multiple of 8): their values
@@ -229,6 +245,12 @@ constexpr int kVtHalf = kVtExps * 128;
 constexpr int kVtBins = 2 * kVtHalf;
 static_assert(kVtBins * (sizeof(double) + sizeof(uint32_t)) <= sizeof(WarpBuf) * kCsWarps,
               "the per-value table overlays the compaction buffers");
+// With top_p < 1 the table's probabilities are never stored: the cut is scanned from the
+// owners' shares and a kept id's probability is one exp. Their area holds, per warp, the
+// offsets of the warp's valid ids in id order (written by the support pass), so the count
+// and kept passes touch valid ids only. A warp with more valid ids than this walks its whole
+// range instead.
+constexpr int kVtListCap = kVtBins * (int)sizeof(double) / (int)sizeof(uint16_t) / kCsWarps;
 
 // largest exponent field among the valid (bit set in `bits`), finite bf16 values of a vector
 // of eight; 0 if none
@@ -270,6 +292,13 @@ __device__ __forceinline__ float vt_value(int b, int e_top) {
 // or for bf16 the per-value table
 __host__ __device__ constexpr int cs_comb_bins(int dt) { return dt == kBF16 ? kVtBins : kCsBins; }
 
+// bins per CTA of the combined area: a share of cs_comb_bins(dt) over k CTAs, rounded up to
+// a multiple of 4 so that four consecutive bins always have one owner and sit 16-byte
+// aligned in its area (vector reads across the cluster)
+__host__ __device__ constexpr int cs_comb_share(int dt, int k) {
+  return ((cs_comb_bins(dt) + k - 1) / k + 3) / 4 * 4;
+}
+
 template <int DT>
 __global__ void __launch_bounds__(kCsThreads, 1)
     masked_sample_cluster_kernel(const ClusterSampleParams p) {
@@ -303,22 +332,49 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   uint32_t* const s_words = p.mask ? reinterpret_cast<uint32_t*>(s_dyn + p.off_words) : nullptr;
   WarpBuf* const s_bufs = reinterpret_cast<WarpBuf*>(s_dyn + p.off_work);
   CsHist* const s_hist = reinterpret_cast<CsHist*>(s_dyn + p.off_work);
-  const int comb_cap = (cs_comb_bins(DT) + k - 1) / k;
+  const int comb_cap = cs_comb_share(DT, k);
   double* const s_comb_p = reinterpret_cast<double*>(s_dyn + p.off_comb);
   uint32_t* const s_comb_c =
       reinterpret_cast<uint32_t*>(s_dyn + p.off_comb + ((comb_cap * 8 + 15) & ~15));
 
-  // 0. stage this CTA's ids: values, then mask words
-  {
-    const St* g = static_cast<const St*>(p.logits) + row * p.row_stride + lo;
-    int j = tid;
-    if (((uintptr_t)g & 15u) == 0) {
-      const int nv = (n * kElem) >> 4;
-      const unsigned char* gb = reinterpret_cast<const unsigned char*>(g);
-      for (int q = tid; q < nv; q += kCsThreads) cs_cp_async16(s_vals + 16 * q, gb + 16 * q);
-      j = nv * (16 / kElem) + tid;
+  // warp w owns the contiguous staged ids [wlo, whi): whole mask words (32 ids each)
+  const int wrange = ((n + 31) / 32 + 31) / 32 * 32;
+  const int wlo = min(n, warp * wrange), whi = min(n, wlo + wrange);
+  // this warp's mask words [wlo / 32, wq1): none for an empty range (wlo = n need not be a
+  // multiple of 32, and the word holding id n - 1 belongs to the warp before)
+  const int wq1 = whi > wlo ? (whi + 31) >> 5 : wlo >> 5;
+  const int wsteps = (whi - wlo + kSampleStep - 1) / kSampleStep;
+  const int spg = (wsteps + kCsStageGroups - 1) / kCsStageGroups;  // steps per copy group
+
+  // 0. stage this CTA's ids, values and mask words. From a 16-byte aligned row every warp
+  //    copies its own range: one group of mask words, then kCsStageGroups groups of values,
+  //    so the support pass starts on the first groups while the others are in flight; otherwise
+  //    every thread copies element by element and the block waits for the whole slice.
+  const St* const g = static_cast<const St*>(p.logits) + row * p.row_stride + lo;
+  const bool warp_staged = ((uintptr_t)g & 15u) == 0;
+  if (warp_staged) {
+    if (p.mask) {
+      const uint32_t* gm = p.mask + row * p.mask_stride + (lo >> 5);
+      for (int q = (wlo >> 5) + lane; q < wq1; q += 32) cs_cp_async4(s_words + q, gm + q);
     }
-    for (; j < n; j += kCsThreads) reinterpret_cast<St*>(s_vals)[j] = __ldg(g + j);
+    cs_cp_async_commit();
+    for (int gi = 0; gi < kCsStageGroups; ++gi) {
+      const int i1 = min(wsteps, (gi + 1) * spg);
+      for (int i = gi * spg; i < i1; ++i) {
+        const int j0 = wlo + i * kSampleStep + 8 * lane;
+        if (j0 + 8 <= whi) {
+#pragma unroll
+          for (int c = 0; c < kElem / 2; ++c)
+            cs_cp_async16(s_vals + (size_t)j0 * kElem + 16 * c,
+                          reinterpret_cast<const unsigned char*>(g + j0) + 16 * c);
+        } else {
+          for (int j = j0; j < whi; ++j) reinterpret_cast<St*>(s_vals)[j] = __ldg(g + j);
+        }
+      }
+      cs_cp_async_commit();
+    }
+  } else {
+    for (int j = tid; j < n; j += kCsThreads) reinterpret_cast<St*>(s_vals)[j] = __ldg(g + j);
     if (p.mask) {
       const uint32_t* gm = p.mask + row * p.mask_stride + (lo >> 5);
       const int nw = (n + 31) >> 5;
@@ -327,10 +383,6 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     cs_cp_async_wait_all();
     __syncthreads();
   }
-
-  // warp w owns the contiguous staged ids [wlo, whi)
-  const int wrange = ((n + 31) / 32 + 7) / 8 * 8;
-  const int wlo = min(n, warp * wrange), whi = min(n, wlo + wrange);
 
   int slot = 0;
   auto exchange = [&](const CsMail& mine) {
@@ -341,14 +393,84 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     slot ^= 1;
   };
 
-  // 1. support: the masked, NaN-propagating maximum (packed pairs for 16-bit types); any
-  //    valid id at all
-  uint32_t any = 0u, lcode, lexp = 0u;
-  {
+  // 1. support: the masked, NaN-propagating maximum; any valid id at all; for bf16 the
+  //    largest finite exponent. bf16 rows with a mask and top_p < 1 first list each warp's
+  //    valid ids, in id order, from its mask words alone (they land first), then take the
+  //    support from the listed ids as their copy groups land. Other rows, and warps with
+  //    more valid ids than a list holds, read every id (packed pairs for 16-bit types).
+  const bool listing = DT == kBF16 && p.top_p < 1.0 && s_words != nullptr;
+  uint16_t* const s_list = reinterpret_cast<uint16_t*>(s_dyn + p.off_work) + warp * kVtListCap;
+  const uint16_t* const s_h = reinterpret_cast<const uint16_t*>(s_vals);
+  uint32_t lcount = 0u;  // this warp's valid ids (warp-uniform); listed while <= kVtListCap
+  uint32_t any = 0u, lcode = 0u, lexp = 0u;
+  bool listed_support = false;
+  if (listing) {
+    if (warp_staged) {
+      cs_cp_async_wait_pending(kCsStageGroups);  // the mask words (the first group)
+      __syncwarp();
+    }
+    for (int qb = wlo >> 5; qb < wq1; qb += 32) {  // warp-uniform: one word per lane
+      const int q = qb + lane;
+      uint32_t bits = 0u;
+      if (q < wq1) {
+        bits = s_words[q];
+        const int left = whi - 32 * q;
+        if (left < 32) bits &= (1u << left) - 1u;
+      }
+      const uint32_t c = __popc(bits);
+      uint32_t incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const uint32_t tot = __shfl_sync(kFull, incl, 31);
+      if (lcount + tot <= (uint32_t)kVtListCap) {
+        uint32_t pos = lcount + incl - c;
+        for (uint32_t mm = bits; mm; mm &= mm - 1u)
+          s_list[pos++] = (uint16_t)(32 * q - wlo + __ffs(mm) - 1);
+      }
+      lcount += tot;
+    }
+    if (lcount <= (uint32_t)kVtListCap) {
+      __syncwarp();  // the list is visible to the whole warp
+      float lmax = -INFINITY;
+      int landed = 0;  // value groups known to have landed
+      for (uint32_t i0 = 0; i0 < lcount; i0 += 32) {  // warp-uniform
+        if (warp_staged) {
+          // the group of the last id of these 32 (the list is in id order)
+          const int need = (int)(s_list[min(lcount - 1u, i0 + 31u)] / kSampleStep) / spg + 1;
+          if (need > landed) {
+            cs_cp_async_wait_pending(kCsStageGroups - need);
+            __syncwarp();
+            landed = need;
+          }
+        }
+        const uint32_t i = i0 + lane;
+        if (i < lcount) {
+          const uint32_t h = s_h[wlo + s_list[i]];
+          lmax = max_nan_f32(lmax, bf16_bits_to_f32(h));
+          const uint32_t e = (h >> 7) & 0xFFu;
+          if (e != 0xFFu) lexp = max(lexp, e);
+        }
+      }
+      any = lcount ? 1u : 0u;
+      lcode = ord32(lmax);  // NaN: the largest code
+      listed_support = true;
+    }
+  }
+  if (!listed_support) {
     float lmax = -INFINITY;
     uint32_t pm = 0u;
     if constexpr (DT != kF32) pm = Packed16<DT>::kNegInfPair;
-    for (int s = wlo; s < whi; s += kSampleStep) {
+    int staged_to = 0, next_group = 0;  // steps [0, staged_to) of this warp have landed
+    for (int s = wlo; s < whi; s += kSampleStep) {  // warp-uniform
+      if (warp_staged && (s - wlo) / kSampleStep >= staged_to) {
+        cs_cp_async_wait_pending(kCsStageGroups - 1 - next_group);
+        __syncwarp();  // every lane's copies of the group are visible to the warp
+        ++next_group;
+        staged_to += spg;
+      }
       const int j0 = s + 8 * lane;
       if (j0 >= whi) continue;
       uint32_t m = s_words ? (s_words[j0 >> 5] >> (j0 & 31)) & 0xFFu : 0xFFu;
@@ -511,6 +633,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     // bf16: the per-value table; steps 5 and 6 then look probabilities up instead of
     // computing exp per id (while use_table holds)
     bool use_table = false;
+    bool lists_ok = listing && lcount <= (uint32_t)kVtListCap;  // this warp's id list
     const int e_top = (int)c_exp;
     double* const s_tp = reinterpret_cast<double*>(s_dyn + p.off_work);  // [kVtBins] p per id
     uint32_t* const s_tc = reinterpret_cast<uint32_t*>(s_dyn + p.off_work + kVtBins * 8);
@@ -522,28 +645,45 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       __syncthreads();
       double fsum = 0.0;
       uint32_t fn = 0u;
-      for (int s = wlo; s < whi; s += kSampleStep) {
-        float v[8];
-        const uint32_t m = cs_load8<DT>(s_vals, s_words, s + 8 * lane, whi, v);
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          if (!((m >> t) & 1u) || v[t] == -INFINITY) continue;
-          const int b = vt_bin(__float_as_uint(v[t]) >> 16, e_top);
-          if (b >= 0) {
+      auto count_small = [&](uint32_t h) {
+        const double w = weight_exact(bf16_bits_to_f32(h));
+        if (w > 0.0) {
+          fsum += w;
+          ++fn;
+        }
+      };
+      if (lists_ok) {
+        for (uint32_t i = lane; i < lcount; i += 32) {
+          const uint32_t h = s_h[wlo + s_list[i]];
+          if (h == 0xFF80u) continue;  // -inf: weight 0
+          const int b = vt_bin(h, e_top);
+          if (b >= 0)
             atomicAdd(&s_tc[b], 1u);
-          } else {
-            const double w = weight_exact(v[t]);
-            if (w > 0.0) {
-              fsum += w;
-              ++fn;
-            }
+          else
+            count_small(h);
+        }
+      } else {
+        for (int s = wlo; s < whi; s += kSampleStep) {
+          float v[8];
+          const uint32_t m = cs_load8<DT>(s_vals, s_words, s + 8 * lane, whi, v);
+          uint32_t small = 0u;  // this lane's ids of the small region among its eight
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            if (!((m >> t) & 1u) || v[t] == -INFINITY) continue;
+            const int b = vt_bin(__float_as_uint(v[t]) >> 16, e_top);
+            if (b >= 0)
+              atomicAdd(&s_tc[b], 1u);
+            else
+              small |= 1u << t;
           }
+          for (; small; small &= small - 1u)  // rare: zeros and tiny magnitudes
+            count_small(s_h[s + 8 * lane + __ffs(small) - 1]);
         }
       }
       cs_cluster_sync();  // every CTA's counts are complete
       // 3u. this CTA's share of the bins: counts summed over the cluster in rank order, one
       //     exp per nonempty bin; zero weights drop out
-      const int per = (kVtBins + k - 1) / k;
+      const int per = comb_cap;
       const int b0 = (int)rank * per, b1 = min(kVtBins, b0 + per);
       double smass = 0.0;
       uint32_t sn = 0u;
@@ -595,28 +735,41 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         small_w += s_all[q].d[1];
         nwt += s_all[q].u[0];
       }
-      // 3v. the whole table in this CTA: probability and count per bin (every remote read of
-      //     the local counts ended at the exchange)
-      for (int b = tid; b < kVtBins; b += kCsThreads) {
-        const int q = b / per, o = b - q * per;
-        const double w = cs_remote(s_comb_p, (uint32_t)q)[o];
-        s_tc[b] = cs_remote(s_comb_c, (uint32_t)q)[o];
-        s_tp[b] = w / total;
+      // 3v. thread t's bins 4t .. 4t+3, read from their owners' shares (every remote read of
+      //     the local counts ended at the exchange). With top_p = 1 nothing is cut: the
+      //     probabilities are stored for the kept-mass and draw passes. Otherwise only the
+      //     cut is taken from them (3w), and a kept id's probability is one exp.
+      static_assert(kVtBins == 4 * kCsThreads, "four bins per thread");
+      double wv[4];
+      uint32_t cb[4];
+      {
+        const int q = 4 * tid / per, o = 4 * tid - q * per;  // one owner for all four
+        const double2* wq = reinterpret_cast<const double2*>(cs_remote(s_comb_p, (uint32_t)q) + o);
+        const double2 w01 = wq[0], w23 = wq[1];
+        const uint4 c4 = *reinterpret_cast<const uint4*>(cs_remote(s_comb_c, (uint32_t)q) + o);
+        wv[0] = w01.x;
+        wv[1] = w01.y;
+        wv[2] = w23.x;
+        wv[3] = w23.y;
+        cb[0] = c4.x;
+        cb[1] = c4.y;
+        cb[2] = c4.z;
+        cb[3] = c4.w;
       }
-      __syncthreads();
-      // 3w. the cut: ranked by value, the bin where the cumulative probability reaches top_p.
-      //     Thread t owns bins 4t .. 4t+3; the small region follows bin kVtHalf - 1. Every
-      //     CTA scans the same table and finds the same cut.
-      if (!keep_all) {
-        static_assert(kVtBins == 4 * kCsThreads, "four bins per thread");
+      if (keep_all) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s_tp[4 * tid + i] = wv[i] / total;
+        __syncthreads();
+      } else {
+        // 3w. the cut: ranked by value, the bin where the cumulative probability reaches
+        //     top_p; the small region follows bin kVtHalf - 1. Every CTA scans the same
+        //     values and finds the same cut.
         const double small_p = small_w / total;
         double pb[4];
-        uint32_t cb[4];
         double tm = 0.0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          cb[i] = s_tc[4 * tid + i];
-          pb[i] = (double)cb[i] * s_tp[4 * tid + i];
+          pb[i] = (double)cb[i] * (wv[i] / total);
           tm += pb[i];
         }
         const bool small_after = 4 * tid + 3 == kVtHalf - 1;
@@ -645,7 +798,8 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         __syncthreads();
         if (mine != 0xFFFFFFFFu && mine == s_bin && !(mine & 1u)) {
           s_above = mine_before;
-          s_ties = cb[(mine >> 1) - 4 * tid];
+          const int i = (int)(mine >> 1) - 4 * tid;  // (a select: no local-memory array)
+          s_ties = i == 0 ? cb[0] : i == 1 ? cb[1] : i == 2 ? cb[2] : cb[3];
         }
         __syncthreads();
         const uint32_t cut = s_bin;
@@ -657,9 +811,11 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         }
         __syncthreads();  // every thread has read s_bin, s_above, s_ties
       }
-      // without a cut here (it falls among the small-region ids, or the sum never reaches
-      // top_p), the radix levels below find it; they overwrite the table
-      if (!have_cut) use_table = false;
+      // the stored probabilities (top_p = 1) serve lookups; without a cut here (it falls
+      // among the small-region ids, or the sum never reaches top_p) the radix levels below
+      // find it, and their histograms overwrite the id lists
+      use_table = keep_all;
+      if (!have_cut) lists_ok = false;
     } else {
       // 3. total weight and the number of weighted ids
       double tsum = 0.0;
@@ -705,15 +861,14 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         nwt += s_all[q].u[0];
       }
     }
-    // candidates: weight >= tau = (1 - top_p) total / (2 n), i.e. value >= vtau; as a float
-    // test, x >= fthr with fthr the least float not below vtau
-    const double tau = (1.0 - p.top_p) * total / (2.0 * (double)nwt);
-    const double vtau = tau > 0.0 ? vmax + p.temperature * log(tau) : -INFINITY;
-    float fthr = (float)vtau;
-    if ((double)fthr < vtau) fthr = nextafterf(fthr, INFINITY);
-
     // 4. radix levels from below the candidates' common prefix down to one exact value
     if (!have_cut) {
+      // candidates: weight >= tau = (1 - top_p) total / (2 n), i.e. value >= vtau; as a
+      // float test, x >= fthr with fthr the least float not below vtau
+      const double tau = (1.0 - p.top_p) * total / (2.0 * (double)nwt);
+      const double vtau = tau > 0.0 ? vmax + p.temperature * log(tau) : -INFINITY;
+      float fthr = (float)vtau;
+      if ((double)fthr < vtau) fthr = nextafterf(fthr, INFINITY);
       const uint32_t lowc = fthr == -INFINITY ? kOrd32NegInf + 1u : min(ord32(fthr), c_maxo);
       const uint32_t diff = lowc ^ c_maxo;
       int top = diff ? 32 - __clz(diff) : 0;  // bits [top, 32) are the same in every candidate
@@ -884,16 +1039,31 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       // lookups, ids of the small region weighted one by one)
       double acc = 0.0;
       uint32_t lane_ties = 0u;
-      for (int s = wlo; s < whi; s += kSampleStep) {
-        float v[8];
-        const uint32_t m = cs_load8<DT>(s_vals, s_words, s + 8 * lane, whi, v);
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          if (!((m >> t) & 1u)) continue;
-          if (v[t] > vstar_f) {
-            acc += prob(v[t]);
-          } else if (!keep_all && v[t] == vstar_f) {
+      if (lists_ok) {
+        for (uint32_t i = lane; i < lcount; i += 32) {
+          const float x = bf16_bits_to_f32(s_h[wlo + s_list[i]]);
+          if (x > vstar_f)
+            acc += prob(x);
+          else if (x == vstar_f)
             ++lane_ties;
+        }
+      } else {
+        for (int s = wlo; s < whi; s += kSampleStep) {
+          float v[8];
+          const uint32_t m = cs_load8<DT>(s_vals, s_words, s + 8 * lane, whi, v);
+          uint32_t kept = 0u;
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            if (!((m >> t) & 1u)) continue;
+            if (v[t] > vstar_f)
+              kept |= 1u << t;
+            else if (!keep_all && v[t] == vstar_f)
+              ++lane_ties;
+          }
+          for (; kept; kept &= kept - 1u) {
+            const int t = __ffs(kept) - 1;
+            acc += prob(bf16_bits_to_f32(
+                reinterpret_cast<const uint16_t*>(s_vals)[s + 8 * lane + t]));
           }
         }
       }

@@ -1603,7 +1603,7 @@ static ClusterSamplePlan cs_layout(int k, int64_t vocab, int dtype, bool masked)
   pl.off_work = (int)off;
   off += sizeof(WarpBuf) * kCsWarps;
   pl.off_comb = (int)off;
-  const size_t cap = (cs_comb_bins(dtype) + k - 1) / k;
+  const size_t cap = (size_t)cs_comb_share(dtype, k);
   off += cs_align16(cap * 8) + cs_align16(cap * 4);
   pl.smem = off;
   return pl;

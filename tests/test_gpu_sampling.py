@@ -72,6 +72,19 @@ def test_full_vocabulary_rows(form, cuda_lib):
     _check(w["logits_bf16"], None, "bf16", 1.0, 0.95, 11, 0)
 
 
+def test_batch_of_full_rows_dense_and_sparse_masks(cuda_lib):
+    """64 full-vocabulary rows, two CTAs per row in the default form: masks from 0.5 % to
+    60 % dense, so some warps work from their list of valid ids and others, with more valid
+    ids than a list holds, walk their whole range; unmasked rows too."""
+    rng = np.random.default_rng(64)
+    x = workloads.normal_bf16(rng, (64, 128256))
+    dens = np.concatenate([rng.uniform(0.005, 0.2, 40), rng.uniform(0.2, 0.6, 24)])
+    m = workloads.bernoulli_masks(rng, dens, 128256)
+    for t, tp, call in ((0.8, 0.9, 0), (0.6, 0.99, 2)):
+        _check(x, m, "bf16", t, tp, 2024, call)
+    _check(x[:8], None, "bf16", 0.8, 0.9, 5, 0)
+
+
 def test_special_rows(form, cuda_lib):
     vocab = 300
     x = np.zeros((8, vocab), np.float32)
