@@ -64,6 +64,13 @@ struct CsMail {
   uint32_t u[4];
 };
 
+struct CsCut {  // a crossing of the per-value table scan
+  double above;   // probability ranked above the cut value
+  double p;       // probability of one id of the cut value
+  uint32_t ties;  // ids of the cut value
+  uint32_t take;  // of those, kept (in id order)
+};
+
 struct CsHist {  // local histogram of one radix level (overlays the compaction buffers)
   double mass[kCsBins];
   uint32_t count[kCsBins];
@@ -251,6 +258,7 @@ static_assert(kVtBins * (sizeof(double) + sizeof(uint32_t)) <= sizeof(WarpBuf) *
 // and kept passes touch valid ids only. A warp with more valid ids than this walks its whole
 // range instead.
 constexpr int kVtListCap = kVtBins * (int)sizeof(double) / (int)sizeof(uint16_t) / kCsWarps;
+constexpr uint32_t kNoList = 0xFFFFFFFFu;
 
 // largest exponent field among the valid (bit set in `bits`), finite bf16 values of a vector
 // of eight; 0 if none
@@ -314,6 +322,9 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   __shared__ uint32_t s_wcount[kCsWarps];  // per warp: +inf ids, then ties of the cut value
   __shared__ uint32_t s_wexp[kCsWarps];    // per warp: largest finite exponent field (bf16)
   __shared__ uint32_t s_bin, s_ties;
+  __shared__ CsCut s_cut[kCsWarps];        // per warp: its earliest crossing of the table scan
+  __shared__ uint32_t s_cutrank[kCsWarps];
+  __shared__ uint32_t s_lcount[kCsWarps];  // per warp: listed ids, kNoList when not listed
   __shared__ double s_above;
   __shared__ long long s_take;
   __shared__ int s_walk_warp;
@@ -459,6 +470,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       listed_support = true;
     }
   }
+  if (lane == 0) s_lcount[warp] = listed_support ? lcount : kNoList;  // (read by this warp)
   if (!listed_support) {
     float lmax = -INFINITY;
     uint32_t pm = 0u;
@@ -630,15 +642,15 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     uint32_t ties = 0u;
     double above = 0.0;  // probability of every id ranked above the current prefix
     bool have_cut = keep_all;  // the cut is known (nothing to cut with top_p = 1)
-    // bf16: the per-value table; steps 5 and 6 then look probabilities up instead of
-    // computing exp per id (while use_table holds)
-    bool use_table = false;
-    bool lists_ok = listing && lcount <= (uint32_t)kVtListCap;  // this warp's id list
+    // bf16: the per-value table. Steps 5 and 6 look a kept id's probability up when its bin
+    // is below lut_bins: every bin with top_p = 1, the positive half otherwise
+    const int lut_bins = DT == kBF16 ? (keep_all ? kVtBins : kVtHalf) : 0;
+    int cut_warp = -1;  // the table scan's crossing (s_cut) also gives pstar and take; -2:
+                        // nothing is cut (top_p = 1)
     const int e_top = (int)c_exp;
     double* const s_tp = reinterpret_cast<double*>(s_dyn + p.off_work);  // [kVtBins] p per id
     uint32_t* const s_tc = reinterpret_cast<uint32_t*>(s_dyn + p.off_work + kVtBins * 8);
     if constexpr (DT == kBF16) {
-      use_table = true;
       // 3t. this CTA's counts per bin (into the count half of the work area) and the per-id
       //     weights of its small-region ids
       for (int b = tid; b < kVtBins; b += kCsThreads) s_tc[b] = 0u;
@@ -652,8 +664,9 @@ __global__ void __launch_bounds__(kCsThreads, 1)
           ++fn;
         }
       };
-      if (lists_ok) {
-        for (uint32_t i = lane; i < lcount; i += 32) {
+      const uint32_t ln = s_lcount[warp];
+      if (ln != kNoList) {
+        for (uint32_t i = lane; i < ln; i += 32) {
           const uint32_t h = s_h[wlo + s_list[i]];
           if (h == 0xFF80u) continue;  // -inf: weight 0
           const int b = vt_bin(h, e_top);
@@ -756,66 +769,82 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         cb[2] = c4.z;
         cb[3] = c4.w;
       }
+      double pv[4];  // probability of one id of each bin
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pv[i] = wv[i] / total;
       if (keep_all) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) s_tp[4 * tid + i] = wv[i] / total;
+        for (int i = 0; i < 4; ++i) s_tp[4 * tid + i] = pv[i];
         __syncthreads();
+        cut_warp = -2;
       } else {
+        // the positive half's probabilities, for lookups, in the area of the local counts
+        // (no CTA reads those any more)
+        double* const s_half = reinterpret_cast<double*>(s_tc);
+        if (4 * tid < kVtHalf) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) s_half[4 * tid + i] = pv[i];
+        }
         // 3w. the cut: ranked by value, the bin where the cumulative probability reaches
         //     top_p; the small region follows bin kVtHalf - 1. Every CTA scans the same
         //     values and finds the same cut.
         const double small_p = small_w / total;
-        double pb[4];
         double tm = 0.0;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          pb[i] = (double)cb[i] * (wv[i] / total);
-          tm += pb[i];
-        }
+        for (int i = 0; i < 4; ++i) tm += (double)cb[i] * pv[i];
         const bool small_after = 4 * tid + 3 == kVtHalf - 1;
         if (small_after) tm += small_p;
         double sum_all;
-        const double before = block_exclusive_scan_d(tm, s_red, &sum_all);
-        if (tid == 0) s_bin = 0xFFFFFFFFu;
-        __syncthreads();
+        const double before = block_exclusive_scan_d(tm, s_red, &sum_all);  // (also orders
+        // the lookup table's stores before any read)
         // the earliest crossing in value order (rank 2b for bin b, 2 kVtHalf - 1 for the small
-        // region); a block-scan rounding could let two threads see one
+        // region); a block-scan rounding could let two threads see one. The crossing thread
+        // also counts the ties the cut keeps, adding them one by one as the reference does.
         double cum = before;
-        uint32_t mine = 0xFFFFFFFFu;
-        double mine_before = 0.0;
+        uint32_t mine = 0xFFFFFFFFu, mine_ties = 0u;
+        double mine_before = 0.0, mine_p = 0.0;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          if (cb[i] && cum < p.top_p && cum + pb[i] >= p.top_p && mine == 0xFFFFFFFFu) {
+          const double pbi = (double)cb[i] * pv[i];
+          if (cb[i] && cum < p.top_p && cum + pbi >= p.top_p && mine == 0xFFFFFFFFu) {
             mine = 2u * (uint32_t)(4 * tid + i);
             mine_before = cum;
+            mine_ties = cb[i];
+            mine_p = pv[i];
           }
-          cum += pb[i];
+          cum += pbi;
         }
         if (small_after && mine == 0xFFFFFFFFu && small_p > 0.0 && cum < p.top_p &&
             cum + small_p >= p.top_p)
           mine = 2u * kVtHalf - 1u;
-        if (mine != 0xFFFFFFFFu) atomicMin(&s_bin, mine);
-        __syncthreads();
-        if (mine != 0xFFFFFFFFu && mine == s_bin && !(mine & 1u)) {
-          s_above = mine_before;
-          const int i = (int)(mine >> 1) - 4 * tid;  // (a select: no local-memory array)
-          s_ties = i == 0 ? cb[0] : i == 1 ? cb[1] : i == 2 ? cb[2] : cb[3];
+        const uint32_t wmin = __reduce_min_sync(kFull, mine);
+        if (mine != 0xFFFFFFFFu && mine == wmin && !(mine & 1u)) {
+          double c2 = mine_before;
+          uint32_t take = mine_ties;
+          for (uint32_t j = 1; j <= mine_ties; ++j) {
+            c2 += mine_p;
+            if (c2 >= p.top_p) {
+              take = j;
+              break;
+            }
+          }
+          s_cut[warp] = CsCut{mine_before, mine_p, mine_ties, take};
         }
+        if (lane == 0) s_cutrank[warp] = wmin;
         __syncthreads();
-        const uint32_t cut = s_bin;
+        const uint32_t r = s_cutrank[lane];
+        const uint32_t cut = __reduce_min_sync(kFull, r);
         if (cut != 0xFFFFFFFFu && !(cut & 1u)) {
+          cut_warp = __ffs(__ballot_sync(kFull, r == cut)) - 1;
           have_cut = true;
           vstar = ord32(vt_value((int)(cut >> 1), e_top));
-          above = s_above;
-          ties = s_ties;
+          above = s_cut[cut_warp].above;
+          ties = s_cut[cut_warp].ties;
         }
-        __syncthreads();  // every thread has read s_bin, s_above, s_ties
       }
-      // the stored probabilities (top_p = 1) serve lookups; without a cut here (it falls
-      // among the small-region ids, or the sum never reaches top_p) the radix levels below
-      // find it, and their histograms overwrite the id lists
-      use_table = keep_all;
-      if (!have_cut) lists_ok = false;
+      // without a cut here (it falls among the small-region ids, or the sum never reaches
+      // top_p) the radix levels below find it; their histograms overwrite the id lists, so
+      // only a cut from this scan (cut_warp >= 0) leaves them for step 5
     } else {
       // 3. total weight and the number of weighted ids
       double tsum = 0.0;
@@ -1006,27 +1035,36 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     // as a float: ord32 order is float order with -0 == +0, and no value here is NaN; with
     // every weighted id kept, -inf is the bound (above it: every finite value)
     const float vstar_f = keep_all ? -INFINITY : cs_code_to_float(vstar);
-    const double pstar = keep_all ? 0.0 : weight_exact(vstar_f) / total;
-    if (tid == 0) {
-      double cum = above;
-      uint32_t take = ties;
-      for (uint32_t j = 1; j <= ties; ++j) {
-        cum += pstar;
-        if (cum >= p.top_p) {
-          take = j;
-          break;
+    double pstar = 0.0;
+    uint32_t take = 0u;
+    if (cut_warp >= 0) {  // (block-uniform)
+      pstar = s_cut[cut_warp].p;
+      take = s_cut[cut_warp].take;
+    } else if (cut_warp == -1) {
+      pstar = keep_all ? 0.0 : weight_exact(vstar_f) / total;
+      if (tid == 0) {
+        double cum = above;
+        uint32_t tk = ties;
+        for (uint32_t j = 1; j <= ties; ++j) {
+          cum += pstar;
+          if (cum >= p.top_p) {
+            tk = j;
+            break;
+          }
         }
+        s_take = tk;
       }
-      s_take = take;
+      __syncthreads();  // (also: every warp is done with the histogram before the buffers)
+      take = (uint32_t)s_take;
     }
-    __syncthreads();  // (also: every warp is done with the histogram before the buffers)
-    const uint32_t take = (uint32_t)s_take;
 
     // probability of one kept id: the table's entry for its value, or exp per id
     auto prob = [&](float x) -> double {
-      if (use_table) {
+      if (lut_bins) {
         const int b = vt_bin(__float_as_uint(x) >> 16, e_top);
-        if (b >= 0) return s_tp[b];
+        if (b >= 0 && b < lut_bins)  // the whole table, or the positive half (top_p < 1)
+          return reinterpret_cast<const double*>(
+              s_dyn + p.off_work + (lut_bins == kVtBins ? 0 : kVtBins * 8))[b];
       }
       return weight_exact(x) / total;
     };
@@ -1039,8 +1077,9 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       // lookups, ids of the small region weighted one by one)
       double acc = 0.0;
       uint32_t lane_ties = 0u;
-      if (lists_ok) {
-        for (uint32_t i = lane; i < lcount; i += 32) {
+      const uint32_t ln = cut_warp >= 0 ? s_lcount[warp] : kNoList;
+      if (ln != kNoList) {
+        for (uint32_t i = lane; i < ln; i += 32) {
           const float x = bf16_bits_to_f32(s_h[wlo + s_list[i]]);
           if (x > vstar_f)
             acc += prob(x);
