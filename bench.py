@@ -2,17 +2,18 @@
 
 Default workload (the headline metric): masked argmax over bf16 logits [64, 128256] with
 per-row uint32 token bitmasks [64, 4008] (density U[0.5%, 20%]). A step is one kernel
-launch over one 64-row batch. Sixteen distinct input sets (279 MB, more than twice the
-126 MB L2) are rotated so every step streams its batch from HBM; the K timed steps are
-replayed from CUDA graphs.
+launch over one 64-row batch. Distinct input sets totalling more than twice the L2 (17
+sets, 297 MB, for the headline) are rotated so every step streams its batch from HBM; the K
+timed steps are replayed from CUDA graphs behind a GPU-side delay.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload batched|spec_verify|table_gather|scaling|vocab_parallel|
                                 dfa_masks|sample|grammar_row]
 
 One process per GPU (torchrun for N > 1). Batches shard over ranks with no communication
-("weak" scaling) except ``vocab_parallel``, which splits the vocabulary and all-gathers
-8-byte keys through NCCL. Rank 0 prints one JSON line.
+("weak" scaling) except ``vocab_parallel``, which splits the vocabulary and exchanges 8-byte
+row keys by NVLink peer stores (``--exchange nccl``: one all-gather). Rank 0 prints one JSON
+line.
 
 ``--impl reference`` times the reference's own selection semantics on the host cores: the
 CPU oracle (a C restatement of the reference's mask + first-max selection, OpenMP over
@@ -46,8 +47,20 @@ FALLBACK_HBM_GBS = 6650.0
 DELAY_CYCLES = 10_000_000
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of each workload's dominant
-# kernel, from a single-launch ncu capture of the current kernels (absent: not captured)
-NCU_TRAFFIC_PER_LAUNCH: dict[str, float] = {}
+# kernel on one B200, from a single-launch ncu capture of that kernel in this program
+# (`--workload <name> --steps 3 --warmup 3`, the fifth launch). The vocabulary-sharded entry
+# is the whole vocabulary on one rank (a rank of N reads 1/N of it); the batch-sharded entry
+# is a launch of 128 rows (traffic grows with the rows).
+NCU_TRAFFIC_PER_LAUNCH: dict[str, float] = {
+    "batched": 17_459_712,
+    "table_gather": 70_165_760,
+    "spec_verify": 52_285_184,
+    "scaling": 69_837_312,
+    "vocab_parallel": 560_186_368,
+    "grammar_row": 147_968,
+    "dfa_masks": 1_756_928,
+    "sample": 17_561_600,
+}
 
 
 # ---------------------------------------------------------------------------------------
@@ -60,10 +73,12 @@ WORKLOADS = {
                          desc="DFA table gather + masked argmax: table u32 [4096,4008], bf16 [256,128256]"),
     "spec_verify": dict(rows=32, vocab=151936, gamma=4,
                         desc="spec verify bf16 [32,5,151936], masks u32 [32,5,4748], drafts i32 [32,4]"),
-    "scaling": dict(rows=128, vocab=256000,
-                    desc="batch-sharded masked argmax bf16 [128/GPU,256000] at 5% density"),
+    "scaling": dict(rows=1024, vocab=256000,
+                    desc="batch-sharded masked argmax bf16 [1024,256000] at 5% density, rows split "
+                         "over N GPUs ([1024/N,256000] each)"),
     "vocab_parallel": dict(rows=1024, vocab=256000,
-                           desc="vocabulary-sharded masked argmax bf16 [1024,256000/N] + NCCL all-gather"),
+                           desc="vocabulary-sharded masked argmax bf16 [1024,256000/N], row keys "
+                                "exchanged between ranks"),
     "grammar_row": dict(rows=1, vocab=32000,
                         desc="one fp32 row [1,32000] under the grammar [0-9]{1,8} at its initial "
                              "state: the valid-token mask built on the GPU from the DFA state, "
@@ -104,6 +119,25 @@ L2_POLICY = {
 }
 
 
+def rows_per_gpu(name: str, world: int) -> int:
+    """Rows one GPU selects per step: the batch-sharded job of 1,024 rows splits over the
+    ranks (strong scaling); every other workload is per GPU."""
+    rows = WORKLOADS[name]["rows"]
+    return rows // world if name == "scaling" else rows
+
+
+def traffic_per_launch(name: str, world: int) -> float | None:
+    """The captured DRAM traffic, scaled to one launch of this run's shard."""
+    t = NCU_TRAFFIC_PER_LAUNCH.get(name)
+    if t is None:
+        return None
+    if name == "vocab_parallel":
+        return t / world
+    if name == "scaling":
+        return t * rows_per_gpu(name, world) / 128
+    return t
+
+
 def workload_config(name: str, world: int, exchange: str) -> dict:
     """The ``config`` object of a JSON line; both arms print the same one."""
     spec = WORKLOADS[name]
@@ -117,7 +151,7 @@ def workload_config(name: str, world: int, exchange: str) -> dict:
     return {
         "workload": name,
         "desc": spec["desc"],
-        "rows_per_step_per_gpu": spec["rows"],
+        "rows_per_step_per_gpu": rows_per_gpu(name, world),
         "parallelism": par,
         "l2_policy": L2_POLICY.get(
             name, "input sets rotate through distinct device buffers totalling more than 2 x L2"),
@@ -362,7 +396,7 @@ def run_reference(args) -> None:
         "steps": args.steps,
         "warmup": args.warmup,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if args.workload in ("vocab_parallel", "scaling") else "weak",
         "vs_baseline": None,
         "dtype": {"dfa_masks": "u32", "grammar_row": "f32"}.get(args.workload, "bf16"),
         "data": "synthetic (seeded, shapes and distributions of the workload)",
@@ -431,7 +465,7 @@ def run_ours(args) -> None:
         w = workloads.spec_verify(gpu_argmax, seed=workloads.SEEDS[3] + seed_shift)
         host_in = {"x": w["logits_bf16"], "m": w["masks"], "d": w["drafts"]}
     elif name == "scaling":
-        w = workloads.scaling(seed=workloads.SEEDS[5] + seed_shift, rows=spec["rows"])
+        w = workloads.scaling(seed=workloads.SEEDS[5] + seed_shift, rows=rows_per_gpu(name, world))
         host_in = {"x": w["logits_bf16"], "m": w["masks"]}
     elif name == "vocab_parallel":
         if args.exchange == "peer":
@@ -456,7 +490,7 @@ def run_ours(args) -> None:
             else:
                 b[k] = torch.from_numpy(np.ascontiguousarray(v)).to(dev)
         bufs.append(b)
-    rows_per_step = spec["rows"]
+    rows_per_step = rows_per_gpu(name, world)
 
     def step(k: int):
         b = bufs[k % R]
@@ -564,13 +598,15 @@ def run_ours(args) -> None:
         "peak": peak,
         "unit": "GB/s",
         "frac": achieved / peak,
-        "traffic": NCU_TRAFFIC_PER_LAUNCH.get(name),
+        "traffic": traffic_per_launch(name, world),
         "peak_source": f"MEASURED_PEAKS.json hbm_gbs (of {peak_kind})",
         "algorithmic_bytes_per_launch": per_launch_bytes,
     }
 
     # ---- end to end through the public API with host buffers ---------------------------
-    e2e_steps = args.steps if name != "vocab_parallel" else min(args.steps, 50)
+    # at least 200 steps (the copy pipeline's first step is not overlapped), bounded by about
+    # 35 GB of host-to-device copies
+    e2e_steps = max(args.steps, 200) if name != "vocab_parallel" else 50
     e2e_steps = min(e2e_steps, max(20, int(2000 * 17.5e6 / max(set_bytes, 1))))
     def _host_view(k, v):
         v = np.ascontiguousarray(v)
@@ -671,7 +707,7 @@ def run_ours(args) -> None:
         "warmup": args.warmup,
         "ms_per_step": ms_per_step,
         "higher_is_better": True,
-        "scaling": "weak" if name != "vocab_parallel" else "strong",
+        "scaling": "strong" if name in ("vocab_parallel", "scaling") else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,3) bf16 logits, Bernoulli token bitmasks)",
@@ -756,7 +792,7 @@ def run_dfa_masks(args) -> None:
     pinned_states = torch.arange(R, dtype=torch.int32).pin_memory()
     host_out = torch.empty((R, out_words), dtype=torch.int32).pin_memory()
     dev_states = torch.empty(R, dtype=torch.int32, device=dev)
-    e2e_steps = min(args.steps, 500)
+    e2e_steps = min(max(args.steps, 200), 500)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         a.record(stream)
@@ -786,7 +822,7 @@ def run_dfa_masks(args) -> None:
                   "behind a GPU-side delay",
         "gbs": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None,
+                     "frac": achieved / peak, "traffic": NCU_TRAFFIC_PER_LAUNCH.get("dfa_masks"),
                      "peak_source": f"MEASURED_PEAKS.json hbm_gbs (of {peak_kind})",
                      "algorithmic_bytes_per_launch": per_launch},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": R * 4,
@@ -914,7 +950,7 @@ def run_grammar_row(args) -> None:
         host_out[0].copy_(r.token_ids, non_blocking=True)
         host_out[1].copy_(r.status, non_blocking=True)
 
-    e2e_steps = min(args.steps, 2000)
+    e2e_steps = min(max(args.steps, 200), 2000)
     with torch.cuda.stream(stream):
         for _ in range(3):
             e2e_step()
@@ -951,7 +987,8 @@ def run_grammar_row(args) -> None:
                   "behind a GPU-side delay; 2 launches per step (mask producer, masked argmax)",
         "gbs": achieved,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None,
+                     "frac": achieved / peak,
+                     "traffic": NCU_TRAFFIC_PER_LAUNCH.get("grammar_row"),  # the argmax launch
                      "peak_source": f"MEASURED_PEAKS.json hbm_gbs (of {peak_kind})",
                      "algorithmic_bytes_per_launch": per_launch},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": V * 4 + 4,

@@ -1215,7 +1215,46 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       }
     }
     __syncthreads();
-    if (warp == s_walk_warp && DT == kBF16) {
+    const uint32_t walk_list = DT == kBF16 && cut_warp >= 0 && warp == s_walk_warp
+                                   ? s_lcount[warp] : kNoList;
+    if (walk_list != kNoList) {
+      // 6. the draw from this warp's list: 32 valid ids at a time, one per lane, in id order;
+      //    running sums by a warp scan
+      double cum = s_walk_before;
+      uint32_t tie_rank = (uint32_t)s_walk_rank;  // ties of the cut value before these ids
+      int pick = -1, last = -1;  // slice-relative
+      for (uint32_t i0 = 0; i0 < walk_list && pick < 0; i0 += 32) {  // warp-uniform
+        const uint32_t i = i0 + lane;
+        int j = -1;
+        float x = -INFINITY;
+        if (i < walk_list) {
+          j = wlo + s_list[i];
+          x = bf16_bits_to_f32(s_h[j]);
+        }
+        const bool tie = x == vstar_f;  // (top_p < 1 here: vstar_f is finite)
+        const unsigned tb = __ballot_sync(kFull, tie);
+        const uint32_t r = tie_rank + __popc(tb & ((1u << lane) - 1u));
+        tie_rank += __popc(tb);
+        const bool keep = x > vstar_f || (tie && r < take);
+        const double pi = keep ? prob(x) : 0.0;
+        double run = pi;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const double t = __shfl_up_sync(kFull, run, o);
+          if (lane >= o) run += t;
+        }
+        const int lastj = (int)__reduce_max_sync(kFull, pi > 0.0 ? (uint32_t)(j + 1) : 0u);
+        if (lastj) last = lastj - 1;
+        const unsigned hit = __ballot_sync(kFull, pi > 0.0 && threshold < cum + run);
+        if (hit) pick = __shfl_sync(kFull, j, __ffs(hit) - 1);
+        cum += __shfl_sync(kFull, run, 31);
+      }
+      if (pick < 0) pick = last;  // the draw lies past this warp's sum (rounding)
+      if (lane == 0) {
+        p.out_idx[row] = (int32_t)(lo + pick);
+        p.out_status[row] = 0u;
+      }
+    } else if (warp == s_walk_warp && DT == kBF16) {
       // 6. the draw: walk this warp's kept ids in id order with running sums; one step of
       //    256 ids at a time, each lane's eight in id order after the lanes before it
       double cum = s_walk_before;
