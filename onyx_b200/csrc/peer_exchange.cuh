@@ -14,9 +14,11 @@
 //   1. the shard-key kernel (key mode) stores row r's key into slot [parity][rank][r] of every
 //      rank's buffer -- plain stores, the peers' over NVLink -- instead of a local key array;
 //   2. exchange_combine_kernel (one CTA, next in the stream) raises this rank's flag to e in
-//      every rank's buffer (fence.acq_rel.sys, then st.release.sys), waits until every flag
-//      in its own buffer is >= e (ld.acquire.sys, bounded), combines the world keys of each
-//      row from its own buffer into the outputs, and stores e as the new epoch count.
+//      every rank's buffer (one fence.acq_rel.sys, then relaxed system-scope stores, all in
+//      flight together), waits until every flag in its own buffer is >= e (lane i of warp 0
+//      polls rank i's flag with ld.acquire.sys, bounded; a block barrier then orders the
+//      whole block after those acquires), combines the world keys of each row from its own
+//      buffer into the outputs, and stores e as the new epoch count.
 // A rank reaches call e + 1's stores only after seeing every rank's flag for e, which every
 // rank raises after its own call e - 1 finished reading; with two parities no store can
 // land in a slot a peer is still reading. Flags only grow, so a rank that has moved on
@@ -49,8 +51,8 @@ struct ExchangeParams {
   uint32_t* out_status;
 };
 
-__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
@@ -64,36 +66,48 @@ __global__ void __launch_bounds__(1024) exchange_combine_kernel(const ExchangePa
   __shared__ unsigned long long s_epoch;
   // the shard-key kernel, and with it this rank's stores into every buffer, has completed
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
     const unsigned long long epoch = __ldcg(e.own_epoch) + 1ull;
-    s_epoch = epoch;
-    bool ok = __ldcg(e.own_failed) == 0ull;
+    bool ok = __ldcg(e.own_failed) == 0ull;  // (the same word for every lane)
     if (ok) {
-      asm volatile("fence.acq_rel.sys;" ::: "memory");
-      for (int i = 0; i < e.world; ++i) st_release_sys_u64(e.flag_dst[i], epoch);
-      const unsigned long long t0 = global_ns();
-      for (int i = 0; i < e.world && ok; ++i) {
-        while (ld_acquire_sys_u64(e.own_flags + i) < epoch) {
+      // release: one system fence, then this rank's flag in every buffer (relaxed stores
+      // after the fence, all in flight at once)
+      if (lane == 0) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        for (int i = 0; i < e.world; ++i) st_relaxed_sys_u64(e.flag_dst[i], epoch);
+      }
+      // acquire: lane i waits for rank i's flag in this rank's buffer, all ranks at once
+      bool arrived = true;
+      if (lane < e.world) {
+        const unsigned long long t0 = global_ns();
+        while (ld_acquire_sys_u64(e.own_flags + lane) < epoch) {
           if (global_ns() - t0 > kExchangeWaitLimitNs) {
-            ok = false;
-            __stcg(e.own_failed, 1ull);  // sticky: later calls neither store nor wait
+            arrived = false;
             break;
           }
         }
       }
+      ok = __all_sync(0xFFFFFFFFu, arrived);
+      if (!ok && lane == 0) __stcg(e.own_failed, 1ull);  // sticky: later calls neither store nor wait
     }
-    s_ok = ok ? 1u : 0u;
+    if (lane == 0) {
+      s_epoch = epoch;
+      s_ok = ok ? 1u : 0u;
+    }
   }
-  __syncthreads();
+  __syncthreads();  // (extends each lane's acquire to the whole block)
   asm volatile("griddepcontrol.launch_dependents;" :::);
   const bool ok = s_ok != 0u;
   const unsigned long long* slots = e.slots + ((s_epoch & 1ull) ? e.parity_stride : 0);
   for (int64_t r = threadIdx.x; r < e.rows; r += blockDim.x) {
+    unsigned long long k[kMaxExchangeRanks];
+#pragma unroll
+    for (int i = 0; i < kMaxExchangeRanks; ++i)
+      k[i] = i < e.world ? __ldcg(slots + (int64_t)i * e.rows_cap + r) : 0ull;
     unsigned long long best = 0ull;
-    for (int i = 0; i < e.world; ++i) {
-      const unsigned long long k = __ldcg(slots + (int64_t)i * e.rows_cap + r);
-      best = k > best ? k : best;
-    }
+#pragma unroll
+    for (int i = 0; i < kMaxExchangeRanks; ++i) best = k[i] > best ? k[i] : best;
     Partial pr;
     pr.flags = (best == kKeyWaitTimeout || !ok ? kFlagWaitTimeout : 0u) | (best ? kFlagAny : 0u);
     pr.ord = best >> 32;
