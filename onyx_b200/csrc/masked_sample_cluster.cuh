@@ -643,8 +643,9 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     double above = 0.0;  // probability of every id ranked above the current prefix
     bool have_cut = keep_all;  // the cut is known (nothing to cut with top_p = 1)
     // bf16: the per-value table. Steps 5 and 6 look a kept id's probability up when its bin
-    // is below lut_bins: every bin with top_p = 1, the positive half otherwise
-    const int lut_bins = DT == kBF16 ? (keep_all ? kVtBins : kVtHalf) : 0;
+    // is below lut_bins: every bin with top_p = 1, the kCsThreads largest positive values
+    // otherwise
+    const int lut_bins = DT == kBF16 ? (keep_all ? kVtBins : kCsThreads) : 0;
     int cut_warp = -1;  // the table scan's crossing (s_cut) also gives pstar and take; -2:
                         // nothing is cut (top_p = 1)
     const int e_top = (int)c_exp;
@@ -700,25 +701,40 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       const int b0 = (int)rank * per, b1 = min(kVtBins, b0 + per);
       double smass = 0.0;
       uint32_t sn = 0u;
-      for (int b = b0 + tid; b < b1; b += kCsThreads) {
-        uint32_t cq[kCsMaxCluster];
+      // (two bins per thread at a time: every remote count read in flight together, and the
+      // two exp chains side by side)
+      for (int b = b0 + tid; b < b1; b += 2 * kCsThreads) {
+        const int b2 = b + kCsThreads;
+        const bool two = b2 < b1;
+        uint32_t c1 = 0u, c2 = 0u;
 #pragma unroll
-        for (int q = 0; q < kCsMaxCluster; ++q) cq[q] = q < k ? cs_remote(s_tc, (uint32_t)q)[b] : 0u;
-        uint32_t csum = 0u;
-#pragma unroll
-        for (int q = 0; q < kCsMaxCluster; ++q) csum += cq[q];
-        double w = 0.0;
-        if (csum) {
-          w = weight_exact(vt_value(b, e_top));
-          if (!(w > 0.0)) {
-            w = 0.0;
-            csum = 0u;
+        for (int q = 0; q < kCsMaxCluster; ++q) {
+          if (q < k) {
+            const uint32_t* rq = cs_remote(s_tc, (uint32_t)q);
+            c1 += rq[b];
+            if (two) c2 += rq[b2];
           }
         }
-        s_comb_p[b - b0] = w;
-        s_comb_c[b - b0] = csum;
-        smass += (double)csum * w;
-        sn += csum;
+        double w1 = c1 ? weight_exact(vt_value(b, e_top)) : 0.0;
+        double w2 = c2 ? weight_exact(vt_value(b2, e_top)) : 0.0;
+        if (!(w1 > 0.0)) {
+          w1 = 0.0;
+          c1 = 0u;
+        }
+        if (!(w2 > 0.0)) {
+          w2 = 0.0;
+          c2 = 0u;
+        }
+        s_comb_p[b - b0] = w1;
+        s_comb_c[b - b0] = c1;
+        smass += (double)c1 * w1;
+        sn += c1;
+        if (two) {
+          s_comb_p[b2 - b0] = w2;
+          s_comb_c[b2 - b0] = c2;
+          smass += (double)c2 * w2;
+          sn += c2;
+        }
       }
       {
         const double wm = warp_sum_d(smass + fsum), wf = warp_sum_d(fsum);
@@ -748,75 +764,32 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         small_w += s_all[q].d[1];
         nwt += s_all[q].u[0];
       }
-      // 3v. thread t's bins 4t .. 4t+3, read from their owners' shares (every remote read of
-      //     the local counts ended at the exchange). With top_p = 1 nothing is cut: the
-      //     probabilities are stored for the kept-mass and draw passes. Otherwise only the
-      //     cut is taken from them (3w), and a kept id's probability is one exp.
-      static_assert(kVtBins == 4 * kCsThreads, "four bins per thread");
-      double wv[4];
-      uint32_t cb[4];
-      {
-        const int q = 4 * tid / per, o = 4 * tid - q * per;  // one owner for all four
+      // 3v. the bins' probabilities, read from their owners' shares (every remote read of the
+      //     local counts ended at the exchange). With top_p = 1 nothing is cut: thread t
+      //     stores bins 4t .. 4t+3 for the kept-mass and draw passes. Otherwise 3w finds the
+      //     cut, and a kept id's probability is a lookup among the top kCsThreads bins or one
+      //     exp.
+      static_assert(kVtBins == 4 * kCsThreads && kCsThreads <= kVtHalf, "bins per thread");
+      // thread t's four bins 4t .. 4t+3 (one owner for all four: shares are multiples of 4)
+      auto load4 = [&](double* pv, uint32_t* cb) {
+        const int q = 4 * tid / per, o = 4 * tid - q * per;
         const double2* wq = reinterpret_cast<const double2*>(cs_remote(s_comb_p, (uint32_t)q) + o);
         const double2 w01 = wq[0], w23 = wq[1];
         const uint4 c4 = *reinterpret_cast<const uint4*>(cs_remote(s_comb_c, (uint32_t)q) + o);
-        wv[0] = w01.x;
-        wv[1] = w01.y;
-        wv[2] = w23.x;
-        wv[3] = w23.y;
+        pv[0] = w01.x / total;
+        pv[1] = w01.y / total;
+        pv[2] = w23.x / total;
+        pv[3] = w23.y / total;
         cb[0] = c4.x;
         cb[1] = c4.y;
         cb[2] = c4.z;
         cb[3] = c4.w;
-      }
-      double pv[4];  // probability of one id of each bin
-#pragma unroll
-      for (int i = 0; i < 4; ++i) pv[i] = wv[i] / total;
-      if (keep_all) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) s_tp[4 * tid + i] = pv[i];
-        __syncthreads();
-        cut_warp = -2;
-      } else {
-        // the positive half's probabilities, for lookups, in the area of the local counts
-        // (no CTA reads those any more)
-        double* const s_half = reinterpret_cast<double*>(s_tc);
-        if (4 * tid < kVtHalf) {
-#pragma unroll
-          for (int i = 0; i < 4; ++i) s_half[4 * tid + i] = pv[i];
-        }
-        // 3w. the cut: ranked by value, the bin where the cumulative probability reaches
-        //     top_p; the small region follows bin kVtHalf - 1. Every CTA scans the same
-        //     values and finds the same cut.
-        const double small_p = small_w / total;
-        double tm = 0.0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) tm += (double)cb[i] * pv[i];
-        const bool small_after = 4 * tid + 3 == kVtHalf - 1;
-        if (small_after) tm += small_p;
-        double sum_all;
-        const double before = block_exclusive_scan_d(tm, s_red, &sum_all);  // (also orders
-        // the lookup table's stores before any read)
-        // the earliest crossing in value order (rank 2b for bin b, 2 kVtHalf - 1 for the small
-        // region); a block-scan rounding could let two threads see one. The crossing thread
-        // also counts the ties the cut keeps, adding them one by one as the reference does.
-        double cum = before;
-        uint32_t mine = 0xFFFFFFFFu, mine_ties = 0u;
-        double mine_before = 0.0, mine_p = 0.0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const double pbi = (double)cb[i] * pv[i];
-          if (cb[i] && cum < p.top_p && cum + pbi >= p.top_p && mine == 0xFFFFFFFFu) {
-            mine = 2u * (uint32_t)(4 * tid + i);
-            mine_before = cum;
-            mine_ties = cb[i];
-            mine_p = pv[i];
-          }
-          cum += pbi;
-        }
-        if (small_after && mine == 0xFFFFFFFFu && small_p > 0.0 && cum < p.top_p &&
-            cum + small_p >= p.top_p)
-          mine = 2u * kVtHalf - 1u;
+      };
+      // the earliest crossing over the block (rank 2b for bin b, 2 kVtHalf - 1 for the small
+      // region; a block-scan rounding could let two threads see one). The crossing thread
+      // also counts the ties the cut keeps, adding them one by one as the reference does.
+      auto publish_cut = [&](uint32_t mine, double mine_before, uint32_t mine_ties,
+                             double mine_p) {
         const uint32_t wmin = __reduce_min_sync(kFull, mine);
         if (mine != 0xFFFFFFFFu && mine == wmin && !(mine & 1u)) {
           double c2 = mine_before;
@@ -840,6 +813,65 @@ __global__ void __launch_bounds__(kCsThreads, 1)
           vstar = ord32(vt_value((int)(cut >> 1), e_top));
           above = s_cut[cut_warp].above;
           ties = s_cut[cut_warp].ties;
+        }
+      };
+      if (keep_all) {
+        double pv[4];
+        uint32_t cb[4];
+        load4(pv, cb);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) s_tp[4 * tid + i] = pv[i];
+        __syncthreads();
+        cut_warp = -2;
+      } else {
+        // 3w, first stage: the kCsThreads largest positive values' bins, one per thread.
+        //     The cut of a top_p < 1 row nearly always lies among them; their probabilities
+        //     become the lookup table (in the area of the local counts, which no CTA reads
+        //     any more).
+        {
+          const int b = tid, q = b / per, o = b - q * per;
+          const double pvb = cs_remote(s_comb_p, (uint32_t)q)[o] / total;
+          const uint32_t c = cs_remote(s_comb_c, (uint32_t)q)[o];
+          reinterpret_cast<double*>(s_tc)[b] = pvb;
+          const double pbb = (double)c * pvb;
+          double sum_all;
+          const double before = block_exclusive_scan_d(pbb, s_red, &sum_all);  // (also orders
+          // the lookup table's stores before any read)
+          const bool cross = c && before < p.top_p && before + pbb >= p.top_p;
+          publish_cut(cross ? 2u * (uint32_t)b : 0xFFFFFFFFu, before, c, pvb);
+        }
+        if (!have_cut) {
+          // second stage: every bin, four per thread, in value order; the small region
+          // follows bin kVtHalf - 1
+          double pv[4];
+          uint32_t cb[4];
+          load4(pv, cb);
+          const double small_p = small_w / total;
+          double tm = 0.0;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) tm += (double)cb[i] * pv[i];
+          const bool small_after = 4 * tid + 3 == kVtHalf - 1;
+          if (small_after) tm += small_p;
+          double sum_all;
+          const double before = block_exclusive_scan_d(tm, s_red, &sum_all);
+          double cum = before;
+          uint32_t mine = 0xFFFFFFFFu, mine_ties = 0u;
+          double mine_before = 0.0, mine_p = 0.0;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const double pbi = (double)cb[i] * pv[i];
+            if (cb[i] && cum < p.top_p && cum + pbi >= p.top_p && mine == 0xFFFFFFFFu) {
+              mine = 2u * (uint32_t)(4 * tid + i);
+              mine_before = cum;
+              mine_ties = cb[i];
+              mine_p = pv[i];
+            }
+            cum += pbi;
+          }
+          if (small_after && mine == 0xFFFFFFFFu && small_p > 0.0 && cum < p.top_p &&
+              cum + small_p >= p.top_p)
+            mine = 2u * kVtHalf - 1u;
+          publish_cut(mine, mine_before, mine_ties, mine_p);
         }
       }
       // without a cut here (it falls among the small-region ids, or the sum never reaches
@@ -1062,7 +1094,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     auto prob = [&](float x) -> double {
       if (lut_bins) {
         const int b = vt_bin(__float_as_uint(x) >> 16, e_top);
-        if (b >= 0 && b < lut_bins)  // the whole table, or the positive half (top_p < 1)
+        if (b >= 0 && b < lut_bins)  // the whole table, or its top (top_p < 1)
           return reinterpret_cast<const double*>(
               s_dyn + p.off_work + (lut_bins == kVtBins ? 0 : kVtBins * 8))[b];
       }
