@@ -659,7 +659,10 @@ def run_ours(args) -> None:
             out_host[j][0].copy_(out[0], non_blocking=True)
             out_host[j][1].copy_(out[1], non_blocking=True)
 
-    for k in range(3):
+    # untimed warm-up of about 10 GB of copies (~0.2 s at the link's rate; the same count on
+    # every rank): a host-to-device link that was idle runs below its rate for the first
+    # tens of milliseconds of traffic
+    for k in range(min(1000, max(3, math.ceil(1e10 / max(h2d, 1))))):
         e2e_step(k)
     torch.cuda.synchronize(dev)
     if distributed:
