@@ -252,12 +252,17 @@ constexpr int kVtHalf = kVtExps * 128;
 constexpr int kVtBins = 2 * kVtHalf;
 static_assert(kVtBins * (sizeof(double) + sizeof(uint32_t)) <= sizeof(WarpBuf) * kCsWarps,
               "the per-value table overlays the compaction buffers");
-// With top_p < 1 the table's probabilities are never stored: the cut is scanned from the
-// owners' shares and a kept id's probability is one exp. Their area holds, per warp, the
-// offsets of the warp's valid ids in id order (written by the support pass), so the count
-// and kept passes touch valid ids only. A warp with more valid ids than this walks its whole
-// range instead.
+// Each warp lists the offsets of its valid ids in id order (written by the support pass), so
+// the count, kept-mass and draw passes touch valid ids only. A warp with more valid ids than
+// a list holds walks its whole range instead.
 constexpr int kVtListCap = kVtBins * (int)sizeof(double) / (int)sizeof(uint16_t) / kCsWarps;
+// bf16 work area: the id lists, then the local counts (until the bin sums), over which the
+// probabilities of the lookup table are stored (the whole table with top_p = 1)
+constexpr int kVtListBytes = kVtListCap * kCsWarps * (int)sizeof(uint16_t);
+constexpr int kVtMinKeepAllSlice = 16384;  // with top_p = 1, smaller slices take exp per id
+constexpr int kVtWorkBytes = kVtListBytes + kVtBins * (int)sizeof(double);
+static_assert(kVtWorkBytes >= (int)(sizeof(WarpBuf) * kCsWarps) &&
+              kVtWorkBytes >= kVtListBytes + kVtBins * (int)sizeof(uint32_t), "bf16 work area");
 constexpr uint32_t kNoList = 0xFFFFFFFFu;
 
 // largest exponent field among the valid (bit set in `bits`), finite bf16 values of a vector
@@ -405,11 +410,11 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   };
 
   // 1. support: the masked, NaN-propagating maximum; any valid id at all; for bf16 the
-  //    largest finite exponent. bf16 rows with a mask and top_p < 1 first list each warp's
+  //    largest finite exponent. bf16 rows with a mask first list each warp's
   //    valid ids, in id order, from its mask words alone (they land first), then take the
   //    support from the listed ids as their copy groups land. Other rows, and warps with
   //    more valid ids than a list holds, read every id (packed pairs for 16-bit types).
-  const bool listing = DT == kBF16 && p.top_p < 1.0 && s_words != nullptr;
+  const bool listing = DT == kBF16 && s_words != nullptr;
   uint16_t* const s_list = reinterpret_cast<uint16_t*>(s_dyn + p.off_work) + warp * kVtListCap;
   const uint16_t* const s_h = reinterpret_cast<const uint16_t*>(s_vals);
   uint32_t lcount = 0u;  // this warp's valid ids (warp-uniform); listed while <= kVtListCap
@@ -645,13 +650,17 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     // bf16: the per-value table. Steps 5 and 6 look a kept id's probability up when its bin
     // is below lut_bins: every bin with top_p = 1, the kCsThreads largest positive values
     // otherwise
-    const int lut_bins = DT == kBF16 ? (keep_all ? kVtBins : kCsThreads) : 0;
+    // the table serves bf16 rows, except with top_p = 1 on small slices, where one exp per
+    // valid id costs less than the table's cluster barriers and reads
+    const bool vt = DT == kBF16 && !(keep_all && p.slice <= kVtMinKeepAllSlice);
+    const int lut_bins = vt ? (keep_all ? kVtBins : kCsThreads) : 0;
     int cut_warp = -1;  // the table scan's crossing (s_cut) also gives pstar and take; -2:
                         // nothing is cut (top_p = 1)
     const int e_top = (int)c_exp;
-    double* const s_tp = reinterpret_cast<double*>(s_dyn + p.off_work);  // [kVtBins] p per id
-    uint32_t* const s_tc = reinterpret_cast<uint32_t*>(s_dyn + p.off_work + kVtBins * 8);
-    if constexpr (DT == kBF16) {
+    // the lookup table: one probability per bin, over the local counts once they are summed
+    double* const s_lut = reinterpret_cast<double*>(s_dyn + p.off_work + kVtListBytes);
+    uint32_t* const s_tc = reinterpret_cast<uint32_t*>(s_dyn + p.off_work + kVtListBytes);
+    if (vt) {
       // 3t. this CTA's counts per bin (into the count half of the work area) and the per-id
       //     weights of its small-region ids
       for (int b = tid; b < kVtBins; b += kCsThreads) s_tc[b] = 0u;
@@ -820,7 +829,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         uint32_t cb[4];
         load4(pv, cb);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) s_tp[4 * tid + i] = pv[i];
+        for (int i = 0; i < 4; ++i) s_lut[4 * tid + i] = pv[i];
         __syncthreads();
         cut_warp = -2;
       } else {
@@ -832,7 +841,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
           const int b = tid, q = b / per, o = b - q * per;
           const double pvb = cs_remote(s_comb_p, (uint32_t)q)[o] / total;
           const uint32_t c = cs_remote(s_comb_c, (uint32_t)q)[o];
-          reinterpret_cast<double*>(s_tc)[b] = pvb;
+          s_lut[b] = pvb;
           const double pbb = (double)c * pvb;
           double sum_all;
           const double before = block_exclusive_scan_d(pbb, s_red, &sum_all);  // (also orders
@@ -876,7 +885,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       }
       // without a cut here (it falls among the small-region ids, or the sum never reaches
       // top_p) the radix levels below find it; their histograms overwrite the id lists, so
-      // only a cut from this scan (cut_warp >= 0) leaves them for step 5
+      // only a cut from this scan (cut_warp >= 0), or none needed (-2), leaves them for step 5
     } else {
       // 3. total weight and the number of weighted ids
       double tsum = 0.0;
@@ -1094,9 +1103,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     auto prob = [&](float x) -> double {
       if (lut_bins) {
         const int b = vt_bin(__float_as_uint(x) >> 16, e_top);
-        if (b >= 0 && b < lut_bins)  // the whole table, or its top (top_p < 1)
-          return reinterpret_cast<const double*>(
-              s_dyn + p.off_work + (lut_bins == kVtBins ? 0 : kVtBins * 8))[b];
+        if (b >= 0 && b < lut_bins) return s_lut[b];  // the whole table, or its top
       }
       return weight_exact(x) / total;
     };
@@ -1104,18 +1111,18 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     // 5. per warp: probability of the ids ranked above the cut value, and the ties
     double wabove = 0.0;
     uint32_t wties = 0u;
-    if (DT == kBF16) {
+    if (vt) {
       // (the per-value path keeps no per-warp totals and no compaction buffers: one pass of
       // lookups, ids of the small region weighted one by one)
       double acc = 0.0;
       uint32_t lane_ties = 0u;
-      const uint32_t ln = cut_warp >= 0 ? s_lcount[warp] : kNoList;
+      const uint32_t ln = cut_warp != -1 ? s_lcount[warp] : kNoList;
       if (ln != kNoList) {
         for (uint32_t i = lane; i < ln; i += 32) {
           const float x = bf16_bits_to_f32(s_h[wlo + s_list[i]]);
           if (x > vstar_f)
             acc += prob(x);
-          else if (x == vstar_f)
+          else if (!keep_all && x == vstar_f)
             ++lane_ties;
         }
       } else {
@@ -1247,7 +1254,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       }
     }
     __syncthreads();
-    const uint32_t walk_list = DT == kBF16 && cut_warp >= 0 && warp == s_walk_warp
+    const uint32_t walk_list = vt && cut_warp != -1 && warp == s_walk_warp
                                    ? s_lcount[warp] : kNoList;
     if (walk_list != kNoList) {
       // 6. the draw from this warp's list: 32 valid ids at a time, one per lane, in id order;
@@ -1263,7 +1270,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
           j = wlo + s_list[i];
           x = bf16_bits_to_f32(s_h[j]);
         }
-        const bool tie = x == vstar_f;  // (top_p < 1 here: vstar_f is finite)
+        const bool tie = !keep_all && x == vstar_f;
         const unsigned tb = __ballot_sync(kFull, tie);
         const uint32_t r = tie_rank + __popc(tb & ((1u << lane) - 1u));
         tie_rank += __popc(tb);
@@ -1286,7 +1293,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
         p.out_idx[row] = (int32_t)(lo + pick);
         p.out_status[row] = 0u;
       }
-    } else if (warp == s_walk_warp && DT == kBF16) {
+    } else if (warp == s_walk_warp && vt) {
       // 6. the draw: walk this warp's kept ids in id order with running sums; one step of
       //    256 ids at a time, each lane's eight in id order after the lanes before it
       double cum = s_walk_before;

@@ -1601,7 +1601,7 @@ static ClusterSamplePlan cs_layout(int k, int64_t vocab, int dtype, bool masked)
   pl.off_words = (int)off;
   if (masked) off += cs_align16((size_t)slice / 32 * 4);
   pl.off_work = (int)off;
-  off += sizeof(WarpBuf) * kCsWarps;
+  off += dtype == kBF16 ? (size_t)kVtWorkBytes : sizeof(WarpBuf) * kCsWarps;
   pl.off_comb = (int)off;
   const size_t cap = (size_t)cs_comb_share(dtype, k);
   off += cs_align16(cap * 8) + cs_align16(cap * 4);
