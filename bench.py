@@ -59,7 +59,7 @@ NCU_TRAFFIC_PER_LAUNCH: dict[str, float] = {
     "vocab_parallel": 560_186_368,
     "grammar_row": 147_968,
     "dfa_masks": 1_756_928,
-    "sample": 17_561_600,
+    "sample": 17_542_912,
 }
 
 
