@@ -4,14 +4,20 @@
 // and the Philox4x32-10 draw); a different decomposition:
 //
 // * One cluster of k CTAs (k = 1..16) per row. CTA r copies ids [r S, min(V, (r + 1) S)) of
-//   the row, values and mask words, into its shared memory once (cp.async, 16-byte copies
-//   when the row is aligned). Every later pass reads shared memory, so a row costs one HBM
-//   read and the passes run on k SMs at once.
+//   the row, values and mask words, into its shared memory once (cp.async; from an aligned
+//   row each warp copies its own range in groups and starts on the first group to land).
+//   Every later pass reads shared memory, so a row costs one HBM read and the passes run on
+//   k SMs at once.
 // * Cluster-wide sums and decisions: each CTA posts its block result in a small mailbox,
 //   the cluster barrier publishes it, and every CTA reads the k mailboxes over distributed
 //   shared memory and combines them in rank order. All CTAs therefore hold bit-identical
 //   totals and take the same branches (the cluster barriers always match up).
-// * The top-p cut. Candidates are the ids of weight at least tau = (1 - top_p) total / (2 n)
+// * bf16 rows with a mask: each warp lists its valid ids from the mask words, and the later
+//   passes run over the lists. The cut comes from a per-value table (one bin per bf16 value
+//   of the row's top 16 exponents, each sign): counts per bin, one exp per nonempty bin, a
+//   block scan over the bins in value order (see "per-value table" below). The radix select
+//   that follows serves the other dtypes, and bf16 rows whose cut falls outside the table.
+// * The top-p cut by radix select. Candidates are the ids of weight at least tau = (1 - top_p) total / (2 n)
 //   (the ids below it weigh at most (1 - top_p) total / 2 together, so the ids above reach
 //   top_p by themselves); in value terms v >= vtau = max + T ln(tau). All candidate order
 //   codes lie between code(vtau) and code(max), so they share the leading bits of those
