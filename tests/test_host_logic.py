@@ -226,3 +226,25 @@ def test_digits_dfa_matches_the_restated_regex_compiler():
             s_mine = int(d["trans"][s_mine, b])
         assert np.array_equal(oracle.dfa_scan_bitmask(mine, s_mine, vocab),
                               oracle.dfa_scan_bitmask(ref, s_ref, vocab))
+
+
+def test_bench_shards_and_records_are_consistent():
+    """The bench's config 5a splits 1,024 rows over the ranks, its traffic figures scale with
+    the shard, and both arms print the same config object."""
+    import bench
+
+    for world in (1, 2, 4, 8):
+        assert bench.rows_per_gpu("scaling", world) * world == 1024
+        assert bench.rows_per_gpu("batched", world) == 64
+        t = bench.traffic_per_launch("vocab_parallel", world)
+        assert t == pytest.approx(bench.NCU_TRAFFIC_PER_LAUNCH["vocab_parallel"] / world)
+        # captured traffic stays within 2 % above the algorithmic bytes of the same launch
+        for name in ("batched", "table_gather", "spec_verify", "scaling", "vocab_parallel"):
+            rows = bench.rows_per_gpu(name, world) if name != "vocab_parallel" else 1024
+            algo = bench.bytes_per_row(name, world) * rows
+            ratio = bench.traffic_per_launch(name, world) / algo
+            assert 1.0 <= ratio < 1.02, (name, world, ratio)
+        cfg = bench.workload_config("scaling", world, "peer")
+        assert cfg["rows_per_step_per_gpu"] == 1024 // world
+        assert cfg == bench.workload_config("scaling", world, "peer")
+    assert bench.traffic_per_launch("no such workload", 1) is None
