@@ -248,3 +248,27 @@ def test_bench_shards_and_records_are_consistent():
         assert cfg["rows_per_step_per_gpu"] == 1024 // world
         assert cfg == bench.workload_config("scaling", world, "peer")
     assert bench.traffic_per_launch("no such workload", 1) is None
+
+
+def test_reference_arm_prints_the_contract_line():
+    """`bench.py --impl reference` times the CPU restatement and prints one JSON line with the
+    GPU arm's metric, unit and config."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    import bench
+
+    root = Path(__file__).resolve().parents[1]
+    out = subprocess.run([sys.executable, str(root / "bench.py"), "--impl", "reference",
+                          "--steps", "2", "--warmup", "3"], cwd=root, capture_output=True,
+                         text=True, timeout=300, check=True).stdout
+    lines = [json.loads(x) for x in out.splitlines() if x.startswith("{")]
+    assert len(lines) == 1
+    line = lines[0]
+    assert line["impl"] == "reference" and line["metric"] == bench.METRIC
+    assert line["unit"] == bench.UNIT and line["higher_is_better"] is True
+    assert line["config"] == bench.workload_config("batched", 1, "peer")
+    assert line["value"] > 0 and line["cpu_baseline"]["kind"] == "port"
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
