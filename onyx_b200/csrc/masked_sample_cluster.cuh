@@ -95,6 +95,13 @@ __device__ __forceinline__ uint32_t cs_rank() {
 
 // generic address of the same shared-memory object in CTA `rank` of the cluster
 template <class T>
+__device__ __forceinline__ T* cs_remote_mut(T* p, uint32_t rank) {
+  unsigned long long out;
+  asm("mapa.u64 %0, %1, %2;" : "=l"(out) : "l"(p), "r"(rank));
+  return reinterpret_cast<T*>(out);
+}
+
+template <class T>
 __device__ __forceinline__ const T* cs_remote(const T* p, uint32_t rank) {
   unsigned long long out;
   asm("mapa.u64 %0, %1, %2;" : "=l"(out) : "l"(p), "r"(rank));
@@ -325,8 +332,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   constexpr int kElem = (int)sizeof(St);
   constexpr int kRb = DT == kBF16 ? 16 : DT == kF16 ? 13 : 0;  // lowest bit a value can set
   extern __shared__ __align__(16) unsigned char s_dyn[];
-  __shared__ CsMail s_mail[2];
-  __shared__ CsMail s_all[kCsMaxCluster];
+  __shared__ CsMail s_box[2][kCsMaxCluster];  // per exchange parity: every CTA's mailbox
   __shared__ double s_red[kSampleWarps];
   __shared__ uint32_t s_u[kSampleWarps];
   __shared__ double s_wmass[kCsWarps];    // per warp: total weight, then kept mass above the cut
@@ -342,6 +348,7 @@ __global__ void __launch_bounds__(kCsThreads, 1)
   __shared__ double s_walk_before;
   __shared__ long long s_walk_rank;
 
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");  // (see exchange)
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int k = p.k;
@@ -406,12 +413,24 @@ __global__ void __launch_bounds__(kCsThreads, 1)
     __syncthreads();
   }
 
+  // Exchange: thread q stores this CTA's mailbox into CTA q's box for this rank, then the
+  // cluster barrier (release / acquire) publishes every box; after it a CTA reads only its own
+  // shared memory, so no CTA ever reads another's after the last exchange. Boxes alternate by
+  // parity: a CTA stores into a box again only after the next barrier, which every CTA
+  // reaches after its last read of that box.
   int slot = 0;
+  const CsMail* s_all = s_box[0];
+  bool first_exchange = true;
   auto exchange = [&](const CsMail& mine) {
-    if (tid == 0) s_mail[slot] = mine;
+    // the first store into another CTA waits for the barrier phase every CTA arrived at when
+    // it started: then every CTA of the cluster is running
+    if (first_exchange) {
+      asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+      first_exchange = false;
+    }
+    if (tid < k) *cs_remote_mut(&s_box[slot][rank], (uint32_t)tid) = mine;
     cs_cluster_sync();
-    if (tid < k) s_all[tid] = *cs_remote(&s_mail[slot], (uint32_t)tid);
-    __syncthreads();
+    s_all = s_box[slot];
     slot ^= 1;
   };
 
@@ -1434,5 +1453,6 @@ __global__ void __launch_bounds__(kCsThreads, 1)
       }
     }
   }
-  cs_cluster_sync();  // no CTA leaves while another may still read its shared memory
+  // (no final cluster barrier: every read of another CTA's shared memory precedes the last
+  // exchange's barrier)
 }
