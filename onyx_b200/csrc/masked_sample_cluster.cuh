@@ -8,10 +8,11 @@
 //   row each warp copies its own range in groups and starts on the first group to land).
 //   Every later pass reads shared memory, so a row costs one HBM read and the passes run on
 //   k SMs at once.
-// * Cluster-wide sums and decisions: each CTA posts its block result in a small mailbox,
-//   the cluster barrier publishes it, and every CTA reads the k mailboxes over distributed
-//   shared memory and combines them in rank order. All CTAs therefore hold bit-identical
-//   totals and take the same branches (the cluster barriers always match up).
+// * Cluster-wide sums and decisions: each CTA stores its block result into every CTA's box
+//   for its rank (distributed shared memory), the cluster barrier publishes the boxes, and
+//   every CTA combines the k boxes from its own shared memory in rank order. All CTAs therefore
+//   hold bit-identical totals and take the same branches (the cluster barriers always match
+//   up).
 // * bf16 rows with a mask: each warp lists its valid ids from the mask words, and the later
 //   passes run over the lists. The cut comes from a per-value table (one bin per bf16 value
 //   of the row's top 16 exponents, each sign): counts per bin, one exp per nonempty bin, a
